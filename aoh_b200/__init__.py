@@ -1,0 +1,24 @@
+"""aoh_b200: B200-native (sm_100a) head-mixed attention runtime and effective-rank
+head classifier, with the API of ernie-research/AoH.
+
+    from aoh_b200 import AoHClassifier, AoHKVCache, aoh_attention
+
+The CUDA kernels live in libaoh.so (built in-tree by ``python -m aoh_b200.build``)
+behind the C ABI of include/aoh.h.
+"""
+from .attention import aoh_attention
+from .cache import AoHKVCache, pages_needed
+from .classifier import AoHClassifier, compute_all_eff_ranks, compute_eff_rank, label_margins
+from .io import load_results, save_results
+
+__all__ = [
+    "AoHClassifier",
+    "AoHKVCache",
+    "aoh_attention",
+    "compute_all_eff_ranks",
+    "compute_eff_rank",
+    "label_margins",
+    "load_results",
+    "pages_needed",
+    "save_results",
+]

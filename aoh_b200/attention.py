@@ -1,0 +1,69 @@
+"""Per-layer head-mixed attention op over the paged cache.
+
+``aoh_attention(cache, layer_idx, q, k, v)`` is the attention core of the
+reference's patched forward (make_aoh_forward, eval/efficiency/
+benchmark_llama31.py:218-250 and benchmark_qwen.py:235-267), from post-RoPE
+q/k/v to the attention output, in ORIGINAL head order:
+
+* retrieval KV heads (label 1) -> ``eager_attention`` over every cached key
+  plus this call's keys, causal when q_len > 1 (:123-132);
+* streaming KV heads (label 0) -> ``streaming_attention`` over the sink +
+  recent window (attention_utils.py:92-119);
+* then ``AoHKVCache.append_layer`` (:171-184), and ``kv_seq_len += q_len``
+  after the last layer (:249-250).
+
+q_len == 1 runs the split-KV decode kernel; longer chunks run the prefill
+kernel.  Both are CUDA kernels in libaoh.so; there is no other path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .cache import AoHKVCache, _check_kv
+
+
+def _check_q(cache: AoHKVCache, q: torch.Tensor, q_len: int) -> None:
+    want = (cache.batch, q_len, cache.num_q_heads, cache.head_dim)
+    if tuple(q.shape) != want:
+        raise ValueError(f"q must have shape (batch, q_len, num_q_heads, head_dim) = {want}, got {tuple(q.shape)}")
+    if q.dtype != cache.dtype or q.device != cache.device or not q.is_contiguous():
+        raise ValueError("q must be a contiguous tensor of the cache's dtype on the cache's device")
+
+
+def aoh_attention(cache: AoHKVCache, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  out: torch.Tensor | None = None, advance: bool = True) -> torch.Tensor:
+    """Attend (retrieval: full, streaming: sink + window), then append k/v.
+
+    q (B, C, Hq, D), k/v (B, C, G, D): contiguous, post-RoPE, original head
+    order, dtype = cache dtype.  Returns (B, C, Hq, D).  With ``advance`` the
+    cache's ``kv_seq_len`` moves by C after the last layer, as the reference
+    does.
+    """
+    if not 0 <= layer_idx < cache.num_layers:
+        raise ValueError(f"layer_idx {layer_idx} out of range")
+    q_len = k.shape[1]
+    _check_kv(cache, k, v)
+    _check_q(cache, q, q_len)
+    if out is None:
+        out = torch.empty_like(q)
+    past = cache.kv_seq_len
+    cache.reserve(past + q_len)
+    L = cache._L
+    st = C.c_void_p(_lib.stream_handle())
+    if q_len == 1:
+        ws = cache.decode_workspace()
+        rc = L.aoh_attn_decode(cache._h, layer_idx, past, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                               C.c_void_p(v.data_ptr()), C.c_void_p(out.data_ptr()),
+                               C.c_void_p(ws.data_ptr()), ws.numel(), st)
+        _lib.check(rc, "aoh_attn_decode")
+    else:
+        rc = L.aoh_attn_prefill(cache._h, layer_idx, past, q_len, C.c_void_p(q.data_ptr()),
+                                C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                                C.c_void_p(out.data_ptr()), st)
+        _lib.check(rc, "aoh_attn_prefill")
+    if advance and layer_idx == cache.num_layers - 1:
+        cache.kv_seq_len += q_len
+    return out

@@ -1,0 +1,424 @@
+// Effective-rank classifier on the GPU.
+//
+// Reference (aoh/effective_rank.py:27-142): for query head h of layer l and its
+// KV group g = h // GRP,
+//     C = (W_Q[h] W_Q[h]^T) (W_K[g] W_K[g]^T)            (d_head x d_head)
+//     lambda = eigvals(C)  (torch.linalg.eigvals, non-symmetric LAPACK geev)
+//     sigma = sqrt(|lambda| + 1e-12); p = sigma / sum(sigma)
+//     eff_rank = exp(-sum p log(p + 1e-12))
+// with sign(W) instead of W in --binary mode (:45-59).  The reference computes
+// in float32 and stores float(fp32) in a float64 array (:85, :139).
+//
+// Here C = QQ.KK with QQ, KK symmetric positive (semi-)definite, so its
+// eigenvalues equal those of the symmetric S = L^T KK L where QQ = L L^T
+// (Cholesky).  Pipeline, all batched over (layer, head):
+//   1. gram_kernel: every QQ_h and KK_g (bf16 rows, products exact in fp32,
+//      fp32 partial sums over 8-element chunks accumulated in fp64; in binary
+//      mode the sums of +-1 products are exact integers);
+//   2. cholesky_kernel: QQ_h = L_h L_h^T in shared memory (fp64);
+//   3. gemm_f64_kernel twice: M = KK_g L_h, S = L_h^T M (fp64);
+//   4. jacobi_kernel: cyclic parallel Jacobi on S (fp64, round-robin pairs,
+//      64 disjoint rotations per step), then the entropy -> effective rank,
+//      rounded to float32 like the reference's stored value.
+// The aggregation over GQA groups and the per-layer top-k stay on the host in
+// float64 exactly as aoh/classifier.py:102-128 does them.
+#include <cfloat>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace aoh {
+namespace {
+
+constexpr int kD = 128;                 // head_dim
+constexpr int kMat = kD * kD;           // elements of one 128x128 matrix
+constexpr int kJPitch = kD + 1;         // padded row (doubles) in the Jacobi kernel
+
+// ---------------------------------------------------------------------------
+// 1. Gram matrices: G = A A^T for A = 128 rows x d_model (bf16), 64x64 tiles.
+// ---------------------------------------------------------------------------
+constexpr int kGT = 64;    // tile
+constexpr int kGK = 32;    // k columns staged per step
+constexpr int kChunk = 8;  // fp32 partial-sum length
+
+__device__ __forceinline__ float wval(__nv_bfloat16 x, bool binary) {
+  const float f = __bfloat162float(x);
+  if (!binary) return f;
+  return (f > 0.f) ? 1.f : ((f < 0.f) ? -1.f : 0.f);
+}
+__device__ __forceinline__ float wval(float f, bool binary) {
+  if (!binary) return f;
+  return (f > 0.f) ? 1.f : ((f < 0.f) ? -1.f : 0.f);
+}
+
+// grid: (3 tiles [00, 01, 11], L * (Hq + G)), 256 threads, 4x4 outputs each.
+// bf16 weights: products are exact in fp32, partial sums over kChunk columns
+// in fp32, accumulated in fp64.  fp32 weights: fp64 products and sums.
+template <typename T>
+__global__ void __launch_bounds__(256) gram_kernel(const T* __restrict__ wq, const T* __restrict__ wk, int Hq,
+                                                   int G, int dm, int binary, double* __restrict__ gram) {
+  __shared__ float sa[kGK][kGT + 4];
+  __shared__ float sb[kGK][kGT + 4];
+  constexpr bool kExactF32 = sizeof(T) == 2;
+  const int tile = blockIdx.x;  // 0: (0,0) 1: (0,1) 2: (1,1)
+  const int ti = tile == 2 ? 1 : 0, tj = tile == 0 ? 0 : 1;
+  const int m = blockIdx.y % (Hq + G), l = blockIdx.y / (Hq + G);
+  const T* A = m < Hq ? wq + ((size_t)l * Hq + m) * kD * dm : wk + ((size_t)l * G + (m - Hq)) * kD * dm;
+  const T* Ar = A + (size_t)ti * kGT * dm;
+  const T* Br = A + (size_t)tj * kGT * dm;
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  double acc[4][4];
+  float part[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0, part[i][j] = 0.f;
+  const bool bin = binary != 0;
+  for (int k0 = 0; k0 < dm; k0 += kGK) {
+    __syncthreads();
+    for (int e = tid; e < kGT * kGK; e += 256) {
+      const int r = e / kGK, c = e % kGK;
+      const bool in = k0 + c < dm;
+      sa[c][r] = in ? wval(Ar[(size_t)r * dm + k0 + c], bin) : 0.f;
+      sb[c][r] = in ? wval(Br[(size_t)r * dm + k0 + c], bin) : 0.f;
+    }
+    __syncthreads();
+    if constexpr (kExactF32) {
+#pragma unroll
+      for (int kc = 0; kc < kGK; kc += kChunk) {
+#pragma unroll
+        for (int kk = kc; kk < kc + kChunk; ++kk) {
+          float a[4], b[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty * 4 + i], b[i] = sb[kk][tx * 4 + i];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) part[i][j] = fmaf(a[i], b[j], part[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] += (double)part[i][j], part[i][j] = 0.f;
+      }
+    } else {
+#pragma unroll 8
+      for (int kk = 0; kk < kGK; ++kk) {
+        double a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty * 4 + i], b[i] = sb[kk][tx * 4 + i];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+      }
+    }
+  }
+  double* Gm = gram + ((size_t)l * (Hq + G) + m) * kMat;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = ti * kGT + ty * 4 + i, c = tj * kGT + tx * 4 + j;
+      Gm[r * kD + c] = acc[i][j];
+      if (ti != tj) Gm[c * kD + r] = acc[i][j];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. Cholesky of every QQ_h in place (lower factor, upper triangle zeroed).
+// A pivot below 1e-13 of the largest diagonal is treated as a zero column
+// (positive semi-definite input), so rank-deficient Grams stay finite.
+// grid: L * Hq, 256 threads, 128 KB shared memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) cholesky_kernel(double* __restrict__ gram, int Hq, int G) {
+  extern __shared__ double sm[];
+  double* A = sm;  // [128][128]
+  __shared__ double s_inv, s_tol;
+  const int l = blockIdx.x / Hq, h = blockIdx.x % Hq;
+  double* Gm = gram + ((size_t)l * (Hq + G) + h) * kMat;
+  const int tid = threadIdx.x;
+  for (int e = tid; e < kMat; e += 256) A[e] = Gm[e];
+  __syncthreads();
+  if (tid == 0) {
+    double mx = 0.0;
+    for (int i = 0; i < kD; ++i) mx = fmax(mx, A[i * kD + i]);
+    s_tol = mx * 1e-13;
+  }
+  __syncthreads();
+  for (int k = 0; k < kD; ++k) {
+    if (tid == 0) {
+      const double d = A[k * kD + k];
+      const double piv = d > s_tol ? sqrt(d) : 0.0;
+      A[k * kD + k] = piv;
+      s_inv = piv > 0.0 ? 1.0 / piv : 0.0;
+    }
+    __syncthreads();
+    for (int i = k + 1 + tid; i < kD; i += 256) A[i * kD + k] *= s_inv;
+    __syncthreads();
+    const int n = kD - k - 1;  // trailing block rows/cols k+1..127, lower triangle
+    for (int e = tid; e < n * n; e += 256) {
+      const int i = k + 1 + e / n, j = k + 1 + e % n;
+      if (j <= i) A[i * kD + j] -= A[i * kD + k] * A[j * kD + k];
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < kMat; e += 256) {
+    const int i = e / kD, j = e % kD;
+    Gm[e] = j <= i ? A[e] : 0.0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. Batched fp64 GEMM, 128x128x128:  C[l,h] = op(A) B
+//    mode 0: M = KK_g L_h   (A = KK_g, B = L_h)
+//    mode 1: S = L_h^T M_h  (A = L_h transposed, B = M_h)
+// grid: (4 tiles of 64x64, L * Hq), 256 threads (4x4 outputs each).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gemm_f64_kernel(const double* __restrict__ gram,
+                                                       const double* __restrict__ mbuf, double* __restrict__ out,
+                                                       int Hq, int G, int mode) {
+  __shared__ double sa[16][kGT + 1];
+  __shared__ double sb[16][kGT + 1];
+  const int l = blockIdx.y / Hq, h = blockIdx.y % Hq;
+  const int grp = Hq / G;
+  const double* Lh = gram + ((size_t)l * (Hq + G) + h) * kMat;
+  const double* KK = gram + ((size_t)l * (Hq + G) + Hq + h / grp) * kMat;
+  const double* Mh = mbuf + ((size_t)l * Hq + h) * kMat;
+  const double* A = mode == 0 ? KK : Lh;
+  const double* Bm = mode == 0 ? Lh : Mh;
+  const bool transA = mode == 1;
+  const int ti = blockIdx.x / 2, tj = blockIdx.x % 2;
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  double acc[4][4] = {};
+  for (int k0 = 0; k0 < kD; k0 += 16) {
+    __syncthreads();
+    for (int e = tid; e < 16 * kGT; e += 256) {
+      const int kk = e / kGT, r = e % kGT;
+      const int row = ti * kGT + r, k = k0 + kk;
+      sa[kk][r] = transA ? A[k * kD + row] : A[row * kD + k];
+      sb[kk][r] = Bm[k * kD + tj * kGT + r];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      double a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty * 4 + i], b[i] = sb[kk][tx * 4 + i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+    }
+  }
+  double* C = out + ((size_t)l * Hq + h) * kMat;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) C[(ti * kGT + ty * 4 + i) * kD + tj * kGT + tx * 4 + j] = acc[i][j];
+}
+
+// ---------------------------------------------------------------------------
+// 4. Parallel cyclic Jacobi on S (symmetric, fp64) -> eigenvalues -> eff rank.
+// Round-robin schedule: in step r the pairs are (127, r) and
+// ((r + k) mod 127, (r - k) mod 127) for k = 1..63 -- 64 disjoint pairs, and
+// over 127 steps every pair exactly once.  Each step computes the 64
+// rotations from the current matrix, applies them to rows, then to columns.
+// Sweeps stop when the off-diagonal norm is below 1e-15 of the diagonal norm.
+// grid: L * Hq, 256 threads, 129x128 doubles of shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kMaxSweeps = 30;
+
+__global__ void __launch_bounds__(256) jacobi_kernel(const double* __restrict__ sbuf, int Hq,
+                                                     double* __restrict__ eff_out) {
+  extern __shared__ double sm[];
+  double* S = sm;  // [128][kJPitch]
+  __shared__ double s_c[64], s_s[64];
+  __shared__ int s_p[64], s_q[64];
+  __shared__ double s_red[8];
+  __shared__ int s_done;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const double* Sg = sbuf + (size_t)blockIdx.x * kMat;
+  for (int e = tid; e < kMat; e += 256) S[(e / kD) * kJPitch + e % kD] = Sg[e];
+  __syncthreads();
+
+  for (int sweep = 0; sweep < kMaxSweeps; ++sweep) {
+    // convergence test: off-diagonal vs diagonal squared norms
+    double off = 0.0, dia = 0.0;
+    for (int e = tid; e < kMat; e += 256) {
+      const int i = e / kD, j = e % kD;
+      const double v = S[i * kJPitch + j];
+      if (i == j) dia += v * v; else off += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      off += __shfl_xor_sync(0xffffffffu, off, o);
+      dia += __shfl_xor_sync(0xffffffffu, dia, o);
+    }
+    if (lane == 0) s_red[warp] = off;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < 8; ++w) t += s_red[w];
+      s_red[0] = t;
+    }
+    __syncthreads();
+    const double off_tot = s_red[0];
+    __syncthreads();
+    if (lane == 0) s_red[warp] = dia;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0.0;
+      for (int w = 0; w < 8; ++w) t += s_red[w];
+      s_done = off_tot <= 1e-30 * t;
+    }
+    __syncthreads();
+    if (s_done) break;
+
+    for (int r = 0; r < kD - 1; ++r) {
+      if (tid < 64) {
+        int p, q;
+        if (tid == 0) {
+          p = r;
+          q = kD - 1;
+        } else {
+          p = (r + tid) % (kD - 1);
+          q = (r - tid + (kD - 1)) % (kD - 1);
+        }
+        if (p > q) { const int t = p; p = q; q = t; }
+        const double app = S[p * kJPitch + p], aqq = S[q * kJPitch + q], apq = S[p * kJPitch + q];
+        double c = 1.0, s = 0.0;
+        if (fabs(apq) > 1e-300 && fabs(apq) > 1e-18 * sqrt(fabs(app * aqq))) {
+          const double theta = (aqq - app) / (2.0 * apq);
+          const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
+          c = 1.0 / sqrt(t * t + 1.0);
+          s = t * c;
+        }
+        s_c[tid] = c;
+        s_s[tid] = s;
+        s_p[tid] = p;
+        s_q[tid] = q;
+      }
+      __syncthreads();
+      // rows: R_p <- c R_p - s R_q ; R_q <- s R_p + c R_q
+      for (int e = tid; e < 64 * kD; e += 256) {
+        const int k = e / kD, j = e % kD;
+        const double c = s_c[k], s = s_s[k];
+        if (s == 0.0) continue;
+        double* rp = S + s_p[k] * kJPitch;
+        double* rq = S + s_q[k] * kJPitch;
+        const double x = rp[j], y = rq[j];
+        rp[j] = c * x - s * y;
+        rq[j] = s * x + c * y;
+      }
+      __syncthreads();
+      // columns
+      for (int e = tid; e < 64 * kD; e += 256) {
+        const int k = e / kD, i = e % kD;
+        const double c = s_c[k], s = s_s[k];
+        if (s == 0.0) continue;
+        double* row = S + i * kJPitch;
+        const int p = s_p[k], q = s_q[k];
+        const double x = row[p], y = row[q];
+        row[p] = c * x - s * y;
+        row[q] = s * x + c * y;
+      }
+      __syncthreads();
+    }
+  }
+
+  // eigenvalues are the diagonal; effective rank (effective_rank.py:77-85) in fp64
+  double sig = 0.0;
+  if (tid < kD) sig = sqrt(fabs(S[tid * kJPitch + tid]) + 1e-12);
+  double ssum = sig;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = ssum;
+  __syncthreads();
+  double total = 0.0;
+  for (int w = 0; w < 8; ++w) total += s_red[w];
+  double hterm = 0.0;
+  if (tid < kD && total >= 1e-12) {
+    const double p = sig / total;
+    hterm = -p * log(p + 1e-12);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) hterm += __shfl_xor_sync(0xffffffffu, hterm, o);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = hterm;
+  __syncthreads();
+  if (tid == 0) {
+    double H = 0.0;
+    for (int w = 0; w < 8; ++w) H += s_red[w];
+    const double eff = total < 1e-12 ? 1.0 : exp(H);
+    eff_out[blockIdx.x] = (double)(float)eff;
+  }
+}
+
+size_t ws_bytes(int L, int Hq, int G) {
+  const size_t gram = (size_t)L * (Hq + G) * kMat * sizeof(double);
+  const size_t mb = (size_t)L * Hq * kMat * sizeof(double);
+  return gram + 2 * mb;
+}
+
+}  // namespace
+}  // namespace aoh
+
+using namespace aoh;
+
+extern "C" {
+
+size_t aoh_classify_workspace_bytes(int32_t num_layers, int32_t num_q_heads, int32_t num_kv_heads,
+                                    int32_t head_dim) {
+  if (num_layers <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim != kD) return 0;
+  return ws_bytes(num_layers, num_q_heads, num_kv_heads);
+}
+
+int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_t L, int32_t Hq, int32_t G,
+                           int32_t head_dim, int32_t d_model, int32_t binary, double* eff_ranks_out, void* workspace,
+                           size_t workspace_bytes, aoh_stream stream) {
+  if (!wq || !wk || !eff_ranks_out || !workspace)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_classify_eff_ranks: null pointer");
+  if (L <= 0 || Hq <= 0 || G <= 0 || d_model <= 0)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_classify_eff_ranks: sizes must be positive");
+  if (Hq % G) return fail(AOH_ERR_INVALID_ARGUMENT, "num_q_heads must be a multiple of num_kv_heads");
+  if (head_dim != kD) return fail(AOH_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", kD, head_dim);
+  if (dtype != AOH_BF16 && dtype != AOH_F32)
+    return fail(AOH_ERR_UNSUPPORTED, "weights must be bf16 or f32 (dtype %d)", dtype);
+  if (workspace_bytes < ws_bytes(L, Hq, G))
+    return fail(AOH_ERR_INVALID_ARGUMENT, "classifier workspace of %zu bytes is smaller than %zu",
+                workspace_bytes, ws_bytes(L, Hq, G));
+  if (reinterpret_cast<uintptr_t>(workspace) % 16)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "classifier workspace must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  double* gram = static_cast<double*>(workspace);
+  double* mbuf = gram + (size_t)L * (Hq + G) * kMat;
+  double* sbuf = mbuf + (size_t)L * Hq * kMat;
+  static bool attrs = false;
+  if (!attrs) {
+    int rc = cuda_check(cudaFuncSetAttribute(cholesky_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kMat * (int)sizeof(double)),
+                        "cholesky smem attribute");
+    if (rc) return rc;
+    rc = cuda_check(cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kD * kJPitch * (int)sizeof(double)),
+                    "jacobi smem attribute");
+    if (rc) return rc;
+    attrs = true;
+  }
+  if (dtype == AOH_BF16)
+    gram_kernel<__nv_bfloat16><<<dim3(3, L * (Hq + G)), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(wq), static_cast<const __nv_bfloat16*>(wk), Hq, G, d_model, binary, gram);
+  else
+    gram_kernel<float><<<dim3(3, L * (Hq + G)), 256, 0, st>>>(static_cast<const float*>(wq),
+                                                              static_cast<const float*>(wk), Hq, G, d_model,
+                                                              binary, gram);
+  cholesky_kernel<<<L * Hq, 256, kMat * sizeof(double), st>>>(gram, Hq, G);
+  gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, mbuf, Hq, G, 0);
+  gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, sbuf, Hq, G, 1);
+  jacobi_kernel<<<L * Hq, 256, kD * kJPitch * sizeof(double), st>>>(sbuf, Hq, eff_ranks_out);
+  return cuda_check(cudaGetLastError(), "classifier kernel launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// Host-side internals shared by the translation units of libaoh.so.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/aoh.h"
+
+namespace aoh {
+
+constexpr int kHeadDim = 128;
+constexpr int kPage = 16;
+
+// Sets the thread's last-error message and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Wraps a CUDA runtime result.
+int cuda_check(cudaError_t e, const char* what);
+
+// Kernel-side view of the cache geometry (passed by value).
+struct CacheGeom {
+  int B, Hq, G, grp, L;
+  int sink, recent, ring_cap, sink_pages, ring_pages;
+  int num_pages;
+  const int32_t* unit_offset;  // device: (L*B*G + 1) offsets into block_table
+  const int32_t* block_table;  // device
+  int32_t* err;                // device check word
+  void* pool;                  // device pool base
+};
+
+}  // namespace aoh
+
+struct aoh_kv_cache {
+  aoh_kv_config cfg{};
+  int64_t elem_bytes = 0;
+  int64_t page_bytes = 0;
+  int32_t n_units = 0;  // L * B * G
+  int32_t sink_pages = 0, ring_pages = 0, ring_cap = 0, ret_cap_pages = 0;
+  std::vector<uint8_t> labels;   // L*G
+  std::vector<uint8_t> owned;    // L*B*G
+  std::vector<int32_t> unit_offset;  // n_units + 1
+  std::vector<int32_t> unit_npages;  // pages granted per unit
+  std::vector<int32_t> table;        // block table mirror, -1 = empty
+  std::vector<int32_t> free_list;    // stack of free page ids
+  int64_t dirty_lo = 0, dirty_hi = 0;  // [lo, hi) in table entries
+  // device
+  void* pool = nullptr;
+  int32_t* dev_base = nullptr;  // tables buffer
+  int32_t* dev_unit_offset = nullptr;
+  int32_t* dev_table = nullptr;
+  int32_t* dev_err = nullptr;
+  bool bound = false;
+  int device = -1;
+  int num_sms = 0;
+  CUtensorMap tmap_pool;  // bf16 pool, 128B-swizzled 64-column boxes
+  bool tmap_ok = false;
+
+  int unit(int layer, int b, int g) const { return (layer * cfg.batch + b) * cfg.num_kv_heads + g; }
+  bool retrieval(int layer, int g) const { return labels[layer * cfg.num_kv_heads + g] != 0; }
+  aoh::CacheGeom geom() const;
+};
+
+namespace aoh {
+// launchers (return aoh_status)
+int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
+                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t decode_workspace_bytes(const aoh_kv_cache* c);
+int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q,
+                        const void* k_new, const void* v_new, void* out, cudaStream_t st);
+int launch_append(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* k_new,
+                  const void* v_new, cudaStream_t st);
+int encode_pool_tmap(aoh_kv_cache* c);
+}  // namespace aoh

@@ -1,0 +1,486 @@
+#!/usr/bin/env python3
+"""Benchmark: head-mixed decode attention, microseconds per layer at 128K context.
+
+Workload (one step = one decode token through every layer's attention):
+  Llama-3.1-8B attention shapes (32 query heads, 8 KV heads, head_dim 128),
+  32 layers, bf16, batch 1 per GPU, 131072-token paged context (16-token
+  pages), 6 of 8 KV heads streaming per layer (labels seeded uniform), sink 128,
+  window 256, KV ~ 0.5*N(0,1), q ~ N(0,1).  Synthetic data (no checkpoint or
+  dataset is needed or available); the cache is filled on the device.
+
+  --gpus N > 1 (one process per GPU, torchrun): N sequences of 128K, the
+  (sequence, KV head) units of every layer partitioned across ranks by the
+  longest-processing-time rule on touched KV tokens; each rank attends its
+  units, then the outputs are all-gathered over NCCL at the layer boundary
+  (weak scaling: per-GPU work is fixed).  ``value`` is microseconds per
+  (layer, sequence) for the whole job.
+
+Also reported on the same line: the decode kernel's HBM roofline fraction,
+an end-to-end number through the public API with host buffers, the CPU
+reference (the oracle's restatement of the reference's eager path) on a
+bounded sample, bf16 prefill TFLOP/s on a bounded sample of the 64K chunked
+prefill, and the classifier's label agreement with the reference.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl aoh|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L_LAYERS, HQ, G, D, T_CTX = 32, 32, 8, 128, 131072
+N_STREAM, SINK, RECENT, KV_SCALE, SEED = 6, 128, 256, 0.5, 0
+METRIC = "decode attn us/layer @128K"
+WORKLOAD = "llama31_8b_decode_128k"
+
+
+# ----------------------------------------------------------------------------
+# helpers
+# ----------------------------------------------------------------------------
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def decode_layer_bytes(T: int, n_ret_units: int, n_str_units: int, B: int) -> int:
+    """Algorithmic HBM bytes of one decode launch (one layer): K+V rows read
+    (retrieval: T cached keys; streaming: min(T, sink+recent)), the new K/V row
+    read once and written once per unit, q read, output written, page ids read."""
+    row = 2 * D * 2  # K + V, bf16
+    kv = n_ret_units * T * row + n_str_units * min(T, SINK + RECENT) * row
+    new = (n_ret_units + n_str_units) * row * 2
+    qo = 2 * B * HQ * D * 2
+    tables = n_ret_units * (-(-T // 16)) * 4 + n_str_units * ((SINK + RECENT) // 16) * 4
+    return kv + new + qo + tables
+
+
+# ----------------------------------------------------------------------------
+# CPU reference (oracle restatement of the reference's eager decode)
+# ----------------------------------------------------------------------------
+
+def cpu_reference_layer_us(n_calls: int, threads: int | None = None):
+    """Time the eager decode of one layer at 128K on the host cores: the
+    reference's AoHKVCache state (full retrieval KV, compressed streaming KV)
+    and its per-layer forward (torch.cat + repeat_kv + fp32 scores + softmax +
+    P.V + append), restated in numpy.  Returns (us per layer call, threads)."""
+    from oracle import aoh_oracle as orc
+    rng = np.random.Generator(np.random.PCG64(SEED))
+    labels = np.ones((1, G))
+    labels[0, :N_STREAM] = 0.0
+    cache = orc.OracleKVCache(1, labels, SINK, RECENT, "bf16")
+    nr, ns = cache.n_ret[0], cache.n_str[0]
+    bf = orc.bf16_round
+    cache.full_k[0] = bf(rng.standard_normal((1, nr, T_CTX, D), dtype=np.float32) * 0.5)
+    cache.full_v[0] = bf(rng.standard_normal((1, nr, T_CTX, D), dtype=np.float32) * 0.5)
+    cache.stream_k[0] = bf(rng.standard_normal((1, ns, SINK + RECENT, D), dtype=np.float32) * 0.5)
+    cache.stream_v[0] = bf(rng.standard_normal((1, ns, SINK + RECENT, D), dtype=np.float32) * 0.5)
+    cache.kv_seq_len = T_CTX
+    q = bf(rng.standard_normal((1, 1, HQ, D), dtype=np.float32))
+    k = bf(rng.standard_normal((1, 1, G, D), dtype=np.float32) * 0.5)
+    v = bf(rng.standard_normal((1, 1, G, D), dtype=np.float32) * 0.5)
+    orc.layer_attention(cache, 0, q, k, v)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(n_calls):
+        orc.layer_attention(cache, 0, q, k, v)
+    dt = (time.perf_counter() - t0) / n_calls
+    return dt * 1e6, threads or os.cpu_count()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n = max(1, args.steps)
+    us, cores = cpu_reference_layer_us(n)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(us * L_LAYERS / 1000, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "layers": L_LAYERS, "batch": 1, "context": T_CTX,
+                   "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
+                         "sample": f"{n} decode calls of one layer at 128K (numpy restatement of the reference's "
+                                   "eager AoHKVCache forward); a step is one layer"},
+        "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def run_aoh(args):
+    import torch
+    import torch.distributed as dist
+
+    import aoh_b200
+    from aoh_b200 import AoHKVCache, aoh_attention, synthetic as syn
+    from aoh_b200 import _lib
+    import ctypes as C
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    B = world  # one 128K sequence per GPU
+    labels = syn.labels_uniform(SEED, L_LAYERS, G, N_STREAM)
+    n_ret_layer = int((labels[0] >= 0.5).sum())
+    # partition (sequence, KV head) units over ranks
+    owner = np.zeros((L_LAYERS, B, G), dtype=np.int32)
+    if world > 1:
+        lab_u8 = np.ascontiguousarray(labels >= 0.5, dtype=np.uint8)
+        _lib.check(_lib.lib().aoh_partition(lab_u8.ctypes.data_as(C.POINTER(C.c_uint8)), L_LAYERS, B, G,
+                                            T_CTX, SINK, RECENT, world,
+                                            owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
+    owned = (owner == rank).astype(np.uint8)
+    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 8
+    cache = AoHKVCache(labels, HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
+                       dtype=torch.bfloat16, device=dev, owned=owned, reserve_all=True)
+    gen = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
+    pv = cache.pool_view()
+    for i in range(0, pv.shape[0], 65536):  # fill the pool in slabs (no large fp32 temporaries)
+        sl = pv[i:i + 65536]
+        sl.copy_((torch.randn(sl.shape, generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16))
+    cache.kv_seq_len = T_CTX
+    q = torch.randn((L_LAYERS, B, 1, HQ, D), generator=gen, device=dev).to(torch.bfloat16)
+    kn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+    vn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+    out = torch.zeros((L_LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
+
+    # gather plumbing (world > 1): pack owned (b, g) head groups, all-gather, unpack
+    if world > 1:
+        grp = HQ // G
+        packs, unpack = [], []
+        max_units = max(int((owner[l] == r).sum()) for l in range(L_LAYERS) for r in range(world))
+        for l in range(L_LAYERS):
+            mine = np.flatnonzero(owner[l].ravel() == rank)
+            idx = np.full(max_units, mine[0] if len(mine) else 0, dtype=np.int64)
+            idx[:len(mine)] = mine
+            packs.append(torch.from_numpy(idx).to(dev))
+            allidx, src = [], []
+            for r in range(world):
+                units = np.flatnonzero(owner[l].ravel() == r)
+                allidx.extend(units.tolist())
+                src.extend((r * max_units + np.arange(len(units))).tolist())
+            unpack.append((torch.tensor(src, device=dev), torch.tensor(allidx, device=dev)))
+        gathered = torch.empty((world * max_units, grp * D), dtype=torch.bfloat16, device=dev)
+
+    def layer(l, q_l, k_l, v_l, o_l):
+        aoh_attention(cache, l, q_l, k_l, v_l, out=o_l)
+        if world > 1:
+            flat = o_l.view(B * G, -1)
+            mine = flat.index_select(0, packs[l])
+            dist.all_gather_into_tensor(gathered, mine)
+            src, dst = unpack[l]
+            flat.index_copy_(0, dst, gathered.index_select(0, src))
+
+    def step():
+        for l in range(L_LAYERS):
+            layer(l, q[l], kn[l], vn[l], out[l])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---------------- device-timed region ----------------
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    torch.cuda.synchronize()
+    T0 = cache.kv_seq_len
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", "") or "")
+    clocks = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or local))
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert cache.device_status() == 0, "device-side check tripped"
+    us_layer_seq = ms * 1000.0 / (L_LAYERS * B)
+
+    # roofline of the decode kernel (the only kernel in the N=1 step)
+    hbm, bf16_peak, peak_src = measured_peaks()
+    T_mid = T0 + args.steps // 2
+    n_ret_units = int(((labels >= 0.5)[:, None, :].repeat(B, 1) & (owned > 0)).sum()) // L_LAYERS
+    n_str_units = int(owned.sum()) // L_LAYERS - n_ret_units
+    bytes_launch = decode_layer_bytes(T_mid, n_ret_units, n_str_units, B)
+    launch_us = ms * 1000.0 / L_LAYERS
+    achieved = bytes_launch / (launch_us * 1e-6) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "decode_bf16_128k_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+        except ValueError:
+            traffic = None
+
+    # ---------------- end to end through the public API, host buffers ----------------
+    e2e = None
+    if args.e2e_steps > 0:
+        qh = q.cpu().pin_memory()
+        kh = kn.cpu().pin_memory()
+        vh = vn.cpu().pin_memory()
+        oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        qd, kd, vd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            for l in range(L_LAYERS):
+                layer(l, qd[l], kd[l], vd[l], out[l])
+            oh.copy_(out, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": round(ems * 1000.0 / (L_LAYERS * B), 2), "unit": "us/layer",
+               "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 2,
+               "d2h_bytes_per_step": int(out.numel()) * 2}
+
+    extras = {}
+    if rank == 0 and world == 1:
+        if not args.no_prefill:
+            extras["prefill"] = prefill_sample(torch, dev, bf16_peak)
+        if not args.no_classifier:
+            extras["labels_exact"] = classifier_check(torch, dev)
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_calls > 0:
+        us_cpu, cores = cpu_reference_layer_us(args.cpu_calls)
+        cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
+               "sample": f"{args.cpu_calls} decode calls of one layer at 128K context (numpy restatement of the "
+                         "reference's eager AoHKVCache forward: cat + repeat_kv + fp32 scores + softmax + P.V + "
+                         "append)"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": round(us_layer_seq, 3), "unit": "us/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "layers": L_LAYERS, "sequences": B, "context": T_CTX,
+                   "q_heads": HQ, "kv_heads": G, "head_dim": D, "page": 16,
+                   "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT,
+                   "parallelism": f"units{world}" if world > 1 else "single",
+                   "l2": f"no flush: {bytes_launch * L_LAYERS / 1e9:.2f} GB of KV per step >> 126 MB L2"},
+        "tokens_per_s": round(B / (ms / 1000.0), 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,
+                     "kernel": "decode_bf16_kernel", "bytes_per_launch": bytes_launch,
+                     "avg_launch_us": round(launch_us, 3)},
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": L_LAYERS * args.steps,
+        "clocks": clk,
+        **extras,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def prefill_sample(torch, dev, bf16_peak):
+    """bf16 prefill TFLOP/s on a bounded sample of the 64K chunked prefill
+    (Qwen2.5-7B shapes, one layer, 2 of 4 KV heads streaming): the last 4096-token
+    chunk at 61440 cached tokens."""
+    from aoh_b200 import AoHKVCache, aoh_attention
+    from aoh_b200.metrics import attention_flops
+    Hq, Gq, past, C = 28, 4, 61440, 4096
+    labels = np.array([[1, 0, 1, 0]], dtype=np.float64)
+    cache = AoHKVCache(labels, Hq, batch=1, max_context=past + C, dtype=torch.bfloat16, device=dev,
+                       reserve_all=True)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    pv = cache.pool_view()
+    pv.copy_(torch.randn(pv.shape, generator=gen, device=dev).to(torch.bfloat16))
+    cache.kv_seq_len = past
+    q = torch.randn((1, C, Hq, D), generator=gen, device=dev).to(torch.bfloat16)
+    k = torch.randn((1, C, Gq, D), generator=gen, device=dev).to(torch.bfloat16)
+    v = torch.randn((1, C, Gq, D), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    for _ in range(2):
+        aoh_attention(cache, 0, q, k, v, out=out, advance=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        aoh_attention(cache, 0, q, k, v, out=out, advance=False)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1000.0 / reps
+    grp = Hq // Gq
+    flops = 2 * grp * (attention_flops(C, past, True, 128, 256) + attention_flops(C, past, False, 128, 256))
+    tf = flops / sec / 1e12
+    return {"tflops": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4), "ms": round(sec * 1e3, 3),
+            "sample": "1 layer, last 4096-token chunk at 61440 cached tokens, Qwen2.5-7B heads, 2/4 streaming",
+            "flops": flops}
+
+
+def classifier_check(torch, dev):
+    """AoH classifier on seeded Qwen2.5-7B-shaped projections (28 layers, 28/4
+    heads, hidden 3584, bf16): GPU effective ranks -> labels vs the reference's
+    labels stored in tests/golden/cls_qwen25_7b.npz, both modes, 3 aggregations
+    x 3 sparsities."""
+    from aoh_b200 import classifier as clf
+    from aoh_b200 import synthetic as syn
+    z = np.load(ROOT / "tests" / "golden" / "cls_qwen25_7b.npz")
+    L, H, Gk, Dh, dm = 28, 28, 4, 128, 3584
+    wq = torch.empty((L, H * Dh, dm), dtype=torch.bfloat16, device=dev)
+    wk = torch.empty((L, Gk * Dh, dm), dtype=torch.bfloat16, device=dev)
+    for l in range(L):
+        a, b = syn.classifier_weights(0, l, H, Gk, Dh, dm)
+        wq[l].copy_(torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16))
+        wk[l].copy_(torch.from_numpy(b.astype(np.int16)).view(torch.bfloat16))
+    res = {}
+    for mode in ("fp32", "binary"):
+        clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ranks = clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")
+        sec = time.perf_counter() - t0
+        match = total = sub_noise = 0
+        for agg in ("mean", "min", "max"):
+            kv = clf.aggregate_kv(ranks, Gk, agg)
+            for sp in (0.25, 0.5, 0.75):
+                lab = clf.labels_from_ranks(kv, sp)
+                want = z[f"{mode}_{agg}_sp{sp}_labels"]
+                margins = clf.label_margins(kv, sp)
+                for l in range(L):
+                    total += 1
+                    if np.array_equal(lab[l], want[l]):
+                        match += 1
+                    elif margins[l] < 2e-6:
+                        sub_noise += 1
+        rel = float(np.max(np.abs(ranks - z[f"{mode}_eff_ranks_q"]) / z[f"{mode}_eff_ranks_q"]))
+        res[mode] = {"layer_decisions_equal": f"{match}/{total}", "differ_below_ref_fp32_noise": sub_noise,
+                     "max_rel_rank_err": rel, "gpu_seconds": round(sec, 4),
+                     "ref_cpu_seconds": round(float(z[f"{mode}_classify_seconds"]), 3)}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["aoh", "reference"], default="aoh")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-calls", type=int, default=10)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-classifier", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "aoh":
+        print("note: --warmup raised to 3", file=sys.stderr)
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_aoh(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

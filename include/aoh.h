@@ -1,0 +1,204 @@
+/*
+ * aoh.h -- C ABI of libaoh.so, the B200 (sm_100a) head-mixed attention runtime
+ * and effective-rank head classifier.
+ *
+ * Plain C: every pointer is either a host pointer or a caller-owned CUDA device
+ * pointer (stated per argument); sizes are in elements unless named *_bytes;
+ * streams are cudaStream_t passed as void*.  Every entry point returns an
+ * aoh_status; on failure aoh_last_error() returns a message for the calling
+ * thread.  No exception crosses this boundary.
+ *
+ * Tensor layouts (row-major, contiguous): q and out (batch, q_len, num_q_heads,
+ * head_dim); k_new and v_new (batch, q_len, num_kv_heads, head_dim) -- the
+ * reference's (bsz, q_len, heads, head_dim) projection views before
+ * .transpose(1, 2), with RoPE already applied (eval/efficiency/
+ * benchmark_llama31.py:204-209).  Heads are in ORIGINAL order: the library is
+ * label-driven and needs no offline weight reordering
+ * (eval/efficiency/reorder_weights.py:19-60 is not required).
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the reference project root).
+ */
+#ifndef AOH_H_
+#define AOH_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AOH_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define AOH_API __attribute__((visibility("default")))
+#else
+#define AOH_API
+#endif
+
+typedef enum {
+  AOH_OK = 0,
+  AOH_ERR_INVALID_ARGUMENT = 1, /* reference: ValueError (benchmark_llama31.py:257-265, classifier.py:41-42) */
+  AOH_ERR_OUT_OF_PAGES = 2,     /* reference: torch.OutOfMemoryError (benchmark_llama31.py:398) */
+  AOH_ERR_CUDA = 3,             /* a CUDA runtime call failed */
+  AOH_ERR_UNSUPPORTED = 4,      /* shape/dtype outside what the kernels implement */
+  AOH_ERR_STATE = 5,            /* reference: RuntimeError (classifier.py:143-144) */
+  AOH_ERR_DEVICE_CHECK = 6      /* a device-side bounds check or bounded wait tripped */
+} aoh_status;
+
+typedef enum { AOH_F32 = 0, AOH_BF16 = 1 } aoh_dtype;
+
+typedef void* aoh_stream; /* cudaStream_t */
+
+/* ABI version of the loaded library (AOH_ABI_VERSION it was built with). */
+AOH_API int aoh_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+AOH_API const char* aoh_last_error(void);
+
+/* ------------------------------------------------------------------------- */
+/* Paged KV cache                                                            */
+/* Replaces AoHKVCache (eval/efficiency/benchmark_llama31.py:135-184;        */
+/* benchmark_qwen.py:144-193): per-layer full KV for retrieval heads, sink + */
+/* recent KV for streaming heads (compress_stream, attention_utils.py:23-42).*/
+/* Here every (layer, sequence, KV head) "unit" owns a list of fixed-size    */
+/* pages in one device pool; retrieval units grow page by page, streaming    */
+/* units own ceil(sink/page) sink pages plus a ring of ceil(recent/page)     */
+/* pages and never more.                                                     */
+/* ------------------------------------------------------------------------- */
+
+typedef struct aoh_kv_cache aoh_kv_cache;
+
+typedef struct {
+  int32_t num_layers;
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;     /* must be 128 */
+  int32_t page_size;    /* must be 16 */
+  int32_t dtype;        /* aoh_dtype */
+  int32_t sink_size;    /* >= 0; reference default 128 */
+  int32_t recent_size;  /* >= 0; reference default 256 */
+  int32_t max_context;  /* tokens per sequence a retrieval unit may hold */
+  int32_t num_pages;    /* pages in the pool */
+  const uint8_t* labels; /* host, (num_layers, num_kv_heads): 1 = retrieval, 0 = streaming */
+  const uint8_t* owned;  /* host, (num_layers, batch, num_kv_heads): 1 = stored here; NULL = all */
+} aoh_kv_config;
+
+/* AoHKVCache.__init__ (benchmark_llama31.py:136-151) + patch_aoh_model's label
+ * validation (:256-266).  Host bookkeeping only; no device memory is touched. */
+AOH_API int aoh_kv_create(const aoh_kv_config* cfg, aoh_kv_cache** out);
+AOH_API void aoh_kv_destroy(aoh_kv_cache* cache);
+
+/* Device buffers the caller must allocate for aoh_kv_bind. */
+AOH_API int aoh_kv_buffer_sizes(const aoh_kv_cache* cache, int64_t* pool_bytes, int64_t* table_bytes);
+
+/* Bind caller-owned device memory (pool: pool_bytes, 1024-byte aligned;
+ * tables: table_bytes, 16-byte aligned) and upload the block tables.
+ * Streaming units receive their sink and ring pages here. */
+AOH_API int aoh_kv_bind(aoh_kv_cache* cache, void* pool, void* tables, aoh_stream stream);
+
+/* Give every retrieval unit of sequence `seq` (-1 = all sequences) the pages
+ * for positions [0, n_tokens).  Host-side; call aoh_kv_sync before the next
+ * kernel that reads the new pages.  AOH_ERR_OUT_OF_PAGES leaves the cache
+ * consistent (pages granted so far stay granted). */
+AOH_API int aoh_kv_reserve(aoh_kv_cache* cache, int32_t seq, int32_t n_tokens);
+
+/* Return all pages of sequence `seq` (-1 = all) to the pool; sequences are
+ * then empty (positions restart at 0). Streaming pages are kept. */
+AOH_API int aoh_kv_release(aoh_kv_cache* cache, int32_t seq);
+
+/* Upload block-table entries changed since the last sync (stream-ordered). */
+AOH_API int aoh_kv_sync(aoh_kv_cache* cache, aoh_stream stream);
+
+/* Pages currently free in the pool. */
+AOH_API int32_t aoh_kv_free_pages(const aoh_kv_cache* cache);
+
+/* Host copy of one unit's page list (for inspection and tests). */
+AOH_API int aoh_kv_unit_pages(const aoh_kv_cache* cache, int32_t layer, int32_t seq, int32_t kv_head,
+                      int32_t* pages, int32_t capacity, int32_t* n_pages);
+
+/* Device byte offset of `position` of unit (layer, seq, kv_head) inside the
+ * pool for the K row (is_value = 0) or V row (1); -1 if not stored. */
+AOH_API int64_t aoh_kv_row_offset(const aoh_kv_cache* cache, int32_t layer, int32_t seq, int32_t kv_head,
+                          int32_t position, int32_t past_len, int32_t is_value);
+
+/* Read and clear the device-side check word (bounds checks, bounded waits);
+ * synchronizes `stream`. *flags == 0 means no check tripped. */
+AOH_API int aoh_kv_device_status(aoh_kv_cache* cache, int32_t* flags, aoh_stream stream);
+
+/* ------------------------------------------------------------------------- */
+/* Attention: attend over (cached keys + this call's keys), then append.     */
+/* Replaces the patched forward's attention core (make_aoh_forward,          */
+/* benchmark_llama31.py:218-250; benchmark_qwen.py:235-267):                 */
+/*   retrieval heads -> eager_attention (:123-132), causal iff q_len > 1,    */
+/*   streaming heads -> streaming_attention (attention_utils.py:92-119),     */
+/*   then AoHKVCache.append_layer (:171-184).                                */
+/* past_len is the reference's kv_cache.kv_seq_len (all sequences equal).    */
+/* Positions [0, past_len + q_len) must be reserved (aoh_kv_reserve + sync). */
+/* ------------------------------------------------------------------------- */
+
+/* Upper bound of the workspace aoh_attn_decode needs (bytes). */
+AOH_API size_t aoh_decode_workspace_bytes(const aoh_kv_cache* cache);
+
+/* Decode step (q_len = 1): split-KV over the paged cache, combine, append.
+ * workspace: caller-owned device memory of aoh_decode_workspace_bytes(),
+ * zero-filled once before its first use; calls sharing a workspace must not
+ * overlap on the GPU. */
+AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len, const void* q,
+                    const void* k_new, const void* v_new, void* out, void* workspace,
+                    size_t workspace_bytes, aoh_stream stream);
+
+/* Prefill chunk (any q_len >= 1): causal attention for retrieval heads,
+ * sink + window for streaming heads, then append. */
+AOH_API int aoh_attn_prefill(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,
+                     const void* q, const void* k_new, const void* v_new, void* out,
+                     aoh_stream stream);
+
+/* AoHKVCache.append_layer alone (benchmark_llama31.py:171-184): write q_len
+ * new tokens at positions past_len.. into every unit of `layer`. */
+AOH_API int aoh_kv_append(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,
+                  const void* k_new, const void* v_new, aoh_stream stream);
+
+/* ------------------------------------------------------------------------- */
+/* Effective-rank classifier                                                 */
+/* Replaces compute_all_eff_ranks / compute_eff_rank                         */
+/* (aoh/effective_rank.py:27-142): per (query head h, KV group h / GRP) the  */
+/* spectrum of C = (W_Q W_Q^T)(W_K W_K^T), turned into an effective rank.    */
+/* ------------------------------------------------------------------------- */
+
+/* wq: device (num_layers, num_q_heads * head_dim, d_model) -- q_proj.weight per layer;
+ * wk: device (num_layers, num_kv_heads * head_dim, d_model) -- k_proj.weight;
+ * dtype: AOH_BF16 or AOH_F32 (the reference upcasts either to float32,
+ * aoh/weight_extract.py:105-111);
+ * eff_ranks_out: device f64 (num_layers, num_q_heads), each value rounded to
+ * float32 as the reference stores float(fp32) (effective_rank.py:85);
+ * binary != 0 uses sign(W) (compute_gram_matrix_binary, :45-59).
+ * workspace: device memory of aoh_classify_workspace_bytes(). */
+AOH_API size_t aoh_classify_workspace_bytes(int32_t num_layers, int32_t num_q_heads, int32_t num_kv_heads,
+                                    int32_t head_dim);
+AOH_API int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_t num_layers, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t d_model, int32_t binary,
+                           double* eff_ranks_out, void* workspace, size_t workspace_bytes,
+                           aoh_stream stream);
+
+/* ------------------------------------------------------------------------- */
+/* Multi-GPU partition (no counterpart in the reference, which only places   */
+/* whole layers with device_map="sequential", benchmark_llama31.py:354-374): */
+/* per layer, longest-processing-time greedy assignment of the (sequence,    */
+/* KV head) units to ranks by touched KV tokens.                             */
+/* ------------------------------------------------------------------------- */
+
+/* labels: host (num_layers, num_kv_heads); owner_out: host (num_layers, batch,
+ * num_kv_heads) rank ids; cost of a unit = context + 1 for retrieval,
+ * min(context, sink + recent) + 1 for streaming. */
+AOH_API int aoh_partition(const uint8_t* labels, int32_t num_layers, int32_t batch, int32_t num_kv_heads,
+                  int32_t context, int32_t sink_size, int32_t recent_size, int32_t n_ranks,
+                  int32_t* owner_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AOH_H_ */

@@ -1,0 +1,154 @@
+"""CUDA attention path vs the reference's outputs (golden fixtures) and vs the
+oracle on seeded inputs, through the C ABI (aoh_attn_prefill / aoh_attn_decode).
+
+Tolerances: 2e-2 absolute for bf16, 1e-4 for float32."""
+import numpy as np
+import pytest
+import torch
+
+from aoh_b200 import AoHKVCache, aoh_attention
+from aoh_b200 import synthetic as syn
+from oracle import aoh_oracle as orc
+from tests import golden_cases as gc
+from tests import gpu_engine as ge
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", gc.ATTN_CASES)
+def test_golden_cases(cuda_device, name):
+    spec, got, ref, ck_ok = gc.replay(name, ge.make_cache, ge.step)
+    assert ck_ok
+    tol = gc.TOL[spec["dtype"]]
+    err = np.abs(got - ref).max()
+    assert err <= tol, f"{name}: max abs err {err} > {tol}"
+
+
+def _run_both(dtype, Hq, G, labels, chunks, decode, sink, recent, seed, batch=1, kv_scale=1.0):
+    """Run the same seeded sequence through the oracle and the CUDA path; return
+    the worst error per step kind."""
+    L = labels.shape[0]
+    total = sum(chunks) + decode
+    inputs = [syn.attn_layer_inputs(seed, l, batch, total, Hq, G, 128, dtype=dtype, kv_scale=kv_scale)
+              for l in range(L)]
+    oc = orc.OracleKVCache(L, labels, sink, recent, dtype)
+    gcache = AoHKVCache(labels, Hq, batch=batch, sink_size=sink, recent_size=recent, max_context=total,
+                        dtype=ge.DTYPES[dtype])
+    errs = {"prefill": 0.0, "decode": 0.0}
+    start = 0
+    for c in list(chunks) + [1] * decode:
+        for l in range(L):
+            q, k, v = (x[:, start:start + c] for x in inputs[l])
+            want = orc.layer_attention(oc, l, q, k, v)
+            got = ge.step(gcache, l, q, k, v)
+            kind = "decode" if c == 1 else "prefill"
+            errs[kind] = max(errs[kind], float(np.abs(got - want).max()))
+        start += c
+    assert gcache.device_status() == 0
+    return errs
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_llama_shapes_against_oracle(cuda_device, dtype):
+    labels = syn.labels_uniform(3, 2, 8, 6)
+    errs = _run_both(dtype, 32, 8, labels, [256, 256, 300], 5, 128, 256, seed=21)
+    tol = gc.TOL[dtype]
+    assert errs["prefill"] <= tol and errs["decode"] <= tol, errs
+
+
+def test_qwen25_group7_batch2(cuda_device):
+    labels = np.array([[1, 0, 0, 1], [0, 0, 0, 1]], dtype=np.float64)
+    errs = _run_both("bf16", 28, 4, labels, [200, 77], 4, 128, 256, seed=22, batch=2)
+    assert max(errs.values()) <= 2e-2, errs
+
+
+@pytest.mark.parametrize("sink,recent", [(0, 0), (0, 40), (7, 0), (16, 16), (130, 250)])
+def test_window_edge_cases(cuda_device, sink, recent):
+    labels = np.array([[0, 1]], dtype=np.float64)
+    for dtype in ("f32", "bf16"):
+        errs = _run_both(dtype, 8, 2, labels, [37, 64, 5], 6, sink, recent, seed=23)
+        assert max(errs.values()) <= gc.TOL[dtype], (dtype, errs)
+
+
+def test_decode_from_empty_cache(cuda_device):
+    # past_len = 0: every head attends to the new key only
+    labels = np.array([[1, 0]], dtype=np.float64)
+    errs = _run_both("bf16", 8, 2, labels, [], 3, 128, 256, seed=24)
+    assert errs["decode"] <= 2e-2
+
+
+def _fill_cache_bf16(cache, layer, k_ctx, v_ctx, chunk=8192):
+    """Write a context straight into the pages (AoHKVCache.append_layer)."""
+    T = k_ctx.shape[1]
+    for s in range(0, T, chunk):
+        e = min(T, s + chunk)
+        cache.kv_seq_len = s
+        cache.append_layer(layer, k_ctx[:, s:e].contiguous(), v_ctx[:, s:e].contiguous())
+    cache.kv_seq_len = T
+
+
+@pytest.mark.parametrize("T", [4096 + 7, 131072])
+def test_long_context_decode_against_oracle(cuda_device, T):
+    """One decode step of a Llama-3.1-8B-shaped layer over a T-token paged
+    context (75% streaming heads), against the oracle on the same data."""
+    Hq, G, B = 32, 8, 1
+    labels = syn.labels_uniform(5, 1, G, 6)
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    k_ctx = (torch.randn((B, T, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    v_ctx = (torch.randn((B, T, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    q = torch.randn((B, 1, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    kn = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    vn = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    cache = AoHKVCache(labels, Hq, batch=B, max_context=T + 1, dtype=torch.bfloat16)
+    _fill_cache_bf16(cache, 0, k_ctx, v_ctx)
+    out = aoh_attention(cache, 0, q, kn, vn)
+    got = out.float().cpu().numpy()
+    f = lambda t: t.float().cpu().numpy()
+    want = orc.decode_from_state(f(q), f(kn), f(vn), f(k_ctx), f(v_ctx), labels[0], T, 128, 256, "bf16")
+    err = np.abs(got - want).max()
+    assert err <= 2e-2, err
+    assert cache.kv_seq_len == T + 1
+    assert cache.device_status() == 0
+    # the new token was appended at position T: a second step sees it
+    q2 = torch.randn((B, 1, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    cache2_k = torch.cat([k_ctx, kn], 1)
+    cache2_v = torch.cat([v_ctx, vn], 1)
+    kn2 = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    vn2 = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    got2 = aoh_attention(cache, 0, q2, kn2, vn2).float().cpu().numpy()
+    want2 = orc.decode_from_state(f(q2), f(kn2), f(vn2), f(cache2_k), f(cache2_v), labels[0], T + 1, 128, 256,
+                                  "bf16")
+    assert np.abs(got2 - want2).max() <= 2e-2
+
+
+def test_streaming_heads_touch_only_their_pages(cuda_device):
+    """A streaming unit owns sink + ring pages only; poisoning every other page
+    of the pool must not change its output."""
+    Hq, G, T = 8, 2, 3000
+    labels = np.array([[0, 0]], dtype=np.float64)
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    k_ctx = (torch.randn((1, T, G, 128), generator=gen, device="cuda")).to(torch.bfloat16)
+    v_ctx = (torch.randn((1, T, G, 128), generator=gen, device="cuda")).to(torch.bfloat16)
+    cache = AoHKVCache(labels, Hq, batch=1, max_context=T + 1, dtype=torch.bfloat16)
+    assert cache.num_pages == 2 * (8 + 16)
+    _fill_cache_bf16(cache, 0, k_ctx, v_ctx, chunk=1000)
+    q = torch.randn((1, 1, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    kn = torch.randn((1, 1, G, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    out = aoh_attention(cache, 0, q, kn, kn, advance=False).float().cpu().numpy()
+    f = lambda t: t.float().cpu().numpy()
+    want = orc.decode_from_state(f(q), f(kn), f(kn), f(k_ctx), f(v_ctx), labels[0], T, 128, 256, "bf16")
+    assert np.abs(out - want).max() <= 2e-2
+
+
+def test_bad_arguments_raise(cuda_device):
+    labels = np.array([[1, 0]], dtype=np.float64)
+    cache = AoHKVCache(labels, 8, max_context=64, dtype=torch.bfloat16)
+    q = torch.zeros((1, 1, 8, 128), dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros((1, 1, 2, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        aoh_attention(cache, 1, q, kv, kv)
+    with pytest.raises(ValueError):
+        aoh_attention(cache, 0, q.float(), kv, kv)
+    cache.kv_seq_len = 64
+    with pytest.raises(torch.OutOfMemoryError):
+        aoh_attention(cache, 0, q, kv, kv)
