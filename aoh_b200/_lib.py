@@ -53,7 +53,7 @@ _SIGNATURES = {
     "aoh_kv_sync": (C.c_int, [_vp, _vp]),
     "aoh_kv_free_pages": (_i32, [_vp]),
     "aoh_kv_unit_pages": (C.c_int, [_vp, _i32, _i32, _i32, C.POINTER(_i32), _i32, C.POINTER(_i32)]),
-    "aoh_kv_row_offset": (_i64, [_vp, _i32, _i32, _i32, _i32, _i32, _i32]),
+    "aoh_kv_locate": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(_i32), C.POINTER(_i32)]),
     "aoh_kv_device_status": (C.c_int, [_vp, C.POINTER(_i32), _vp]),
     "aoh_decode_workspace_bytes": (C.c_size_t, [_vp]),
     "aoh_attn_decode": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, C.c_size_t, _vp]),

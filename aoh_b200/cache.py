@@ -109,7 +109,8 @@ class AoHKVCache:
         pool_b, tab_b = C.c_int64(), C.c_int64()
         _lib.check(self._L.aoh_kv_buffer_sizes(h, C.byref(pool_b), C.byref(tab_b)))
         # pool aligned to 1024 B (TMA swizzle atoms); torch's allocator gives >= 512 B, so over-allocate
-        self._pool_raw = torch.empty(pool_b.value + 1024, dtype=torch.uint8, device=self.device)
+        # zero-filled: slots not yet written never hold NaN/Inf bit patterns
+        self._pool_raw = torch.zeros(pool_b.value + 1024, dtype=torch.uint8, device=self.device)
         off = (-self._pool_raw.data_ptr()) % 1024
         self.pool = self._pool_raw[off:off + pool_b.value]
         self.tables = torch.zeros(tab_b.value, dtype=torch.uint8, device=self.device)
@@ -149,9 +150,31 @@ class AoHKVCache:
         _lib.check(self._L.aoh_kv_unit_pages(self._h, layer, seq, kv_head, buf, n.value, C.byref(n)))
         return list(buf[: n.value])
 
-    def row_offset(self, layer: int, seq: int, kv_head: int, position: int, is_value: bool) -> int:
-        return int(self._L.aoh_kv_row_offset(self._h, layer, seq, kv_head, position,
-                                              self.kv_seq_len, int(is_value)))
+    def locate(self, layer: int, seq: int, kv_head: int, position: int) -> tuple[int, int]:
+        """(page, slot) holding ``position`` of a unit, (-1, -1) if not held."""
+        pg, sl = C.c_int32(), C.c_int32()
+        _lib.check(self._L.aoh_kv_locate(self._h, layer, seq, kv_head, position, self.kv_seq_len,
+                                         C.byref(pg), C.byref(sl)))
+        return int(pg.value), int(sl.value)
+
+    def read_rows(self, layer: int, seq: int, kv_head: int, positions) -> tuple[torch.Tensor, torch.Tensor]:
+        """K and V rows (len(positions), head_dim) as stored in the pool
+        (inspection/tests; decodes the bf16 page swizzle)."""
+        pv = self.pool_view()
+        ks, vs = [], []
+        d = torch.arange(self.head_dim, device=self.device)
+        for p in positions:
+            pg, sl = self.locate(layer, seq, kv_head, int(p))
+            if pg < 0:
+                raise KeyError(f"position {p} of unit ({layer}, {seq}, {kv_head}) is not stored")
+            flat = pv[pg].reshape(-1)
+            for kv, acc in ((0, ks), (1, vs)):
+                if self.dtype == torch.bfloat16:
+                    idx = ((d >> 6) * 2048 + kv * 1024 + sl * 64 + (((d >> 3) & 7) ^ (sl & 7)) * 8 + (d & 7))
+                else:
+                    idx = (kv * PAGE_SIZE + sl) * self.head_dim + d
+                acc.append(flat[idx])
+        return torch.stack(ks), torch.stack(vs)
 
     def pool_view(self) -> torch.Tensor:
         """The pool as (num_pages, 2, 16, head_dim) of the cache dtype."""

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "page_layout.cuh"
 
 namespace aoh {
 namespace {
@@ -29,12 +30,14 @@ template <typename T>
 struct Elem;
 template <>
 struct Elem<float> {
+  __device__ static int page_off(int kv, int slot, int d) { return f32_elem_offset(kv, slot, d); }
   __device__ static float ld(const float* p) { return *p; }
   __device__ static float rnd(float x) { return x; }
   __device__ static void st(float* p, float x) { *p = x; }
 };
 template <>
 struct Elem<__nv_bfloat16> {
+  __device__ static int page_off(int kv, int slot, int d) { return bf16_elem_offset(kv, slot, d); }
   __device__ static float ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
   __device__ static float rnd(float x) { return __bfloat162float(__float2bfloat16(x)); }
   __device__ static void st(__nv_bfloat16* p, float x) { *p = __float2bfloat16(x); }
@@ -132,6 +135,7 @@ __global__ void __launch_bounds__(kGThreads) attn_generic_kernel(const GenericAr
       int pos = -1;
       const T* kp = nullptr;
       const T* vp = nullptr;
+      float kval = 0.f, vval = 0.f;
       if (t < n_tiles_cache) {
         const int key = t * kKeyTile + j;
         if (key < n_cache_keys) {
@@ -145,8 +149,8 @@ __global__ void __launch_bounds__(kGThreads) attn_generic_kernel(const GenericAr
               pos = -1;
             } else {
               const T* page = static_cast<const T*>(G.pool) + (size_t)pid * (2 * kPage * kHeadDim);
-              kp = page + (size_t)s * kHeadDim;
-              vp = page + (size_t)(kPage + s) * kHeadDim;
+              kval = E::ld(page + E::page_off(0, s, d));
+              vval = E::ld(page + E::page_off(1, s, d));
             }
           }
         }
@@ -164,10 +168,12 @@ __global__ void __launch_bounds__(kGThreads) attn_generic_kernel(const GenericAr
           const size_t off = (((size_t)b * a.C + i) * G.G + g) * kHeadDim;
           kp = static_cast<const T*>(a.k_new) + off;
           vp = static_cast<const T*>(a.v_new) + off;
+          kval = E::ld(kp + d);
+          vval = E::ld(vp + d);
         }
       }
-      sk[j][d] = kp ? E::ld(kp + d) : 0.f;
-      sv[j][d] = vp ? E::ld(vp + d) : 0.f;
+      sk[j][d] = kval;
+      sv[j][d] = vval;
       if (d == 0) skp[j] = pos;
     }
     __syncthreads();
@@ -267,21 +273,19 @@ __global__ void __launch_bounds__(128) append_kernel(const AppendArgs a) {
     return;
   }
   const size_t src_off = (((size_t)b * a.C + i) * G.G + g) * kHeadDim;
-  T* page = static_cast<T*>(G.pool) + (size_t)pid * (2 * kPage * kHeadDim);
-  constexpr int kVec = 16 / sizeof(T);   // elements per 16-byte vector
-  constexpr int kLanes = kHeadDim / kVec;  // lanes per row
-  const int kv = lane / kLanes;
-  if (kv < 2) {
-    const int part = lane % kLanes;
+  uint8_t* page = static_cast<uint8_t*>(G.pool) + (size_t)pid * (2 * kPage * kHeadDim * sizeof(T));
+  if (sizeof(T) == 2) {
+    // bf16: lanes 0-15 write K, 16-31 write V, one 16-byte chunk each (pre-swizzled layout)
+    const int kv = lane >> 4, c8 = lane & 15;
     const T* src = static_cast<const T*>(kv ? a.v_new : a.k_new) + src_off;
-    T* dst = page + ((size_t)kv * kPage + slot) * kHeadDim;
-    reinterpret_cast<uint4*>(dst)[part] = reinterpret_cast<const uint4*>(src)[part];
-  }
-  if (kLanes == 32) {  // float32: one lane per 16 bytes of a row -> second pass for V
-    const int part = lane;
-    const T* src = static_cast<const T*>(a.v_new) + src_off;
-    T* dst = page + ((size_t)kPage + slot) * kHeadDim;
-    reinterpret_cast<uint4*>(dst)[part] = reinterpret_cast<const uint4*>(src)[part];
+    *reinterpret_cast<uint4*>(page + bf16_chunk_offset(kv, slot, c8)) = reinterpret_cast<const uint4*>(src)[c8];
+  } else {
+    // f32: row-major rows of 512 bytes, one 16-byte chunk per lane, K then V
+    for (int kv = 0; kv < 2; ++kv) {
+      const T* src = static_cast<const T*>(kv ? a.v_new : a.k_new) + src_off;
+      uint8_t* dst = page + (size_t)f32_elem_offset(kv, slot, 0) * sizeof(float);
+      reinterpret_cast<uint4*>(dst)[lane] = reinterpret_cast<const uint4*>(src)[lane];
+    }
   }
 }
 

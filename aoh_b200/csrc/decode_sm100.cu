@@ -15,23 +15,30 @@
 // never read.
 //
 // CTA = 1 producer warp + 4 consumer warps.
-//   producer: lane 0 issues two TMA tensor loads per page (64-dim halves of K
-//     and V, 128B-swizzled) into an 8-stage shared-memory ring guarded by
-//     mbarriers; page ids are fetched 32 at a time by the whole warp.
+//   producer: lane 0 issues one 8 KB bulk copy (cp.async.bulk) per page into
+//     an 8-stage shared-memory ring guarded by mbarriers -- pages are stored
+//     pre-swizzled (page_layout.cuh), so the copy lands in the 128-byte
+//     swizzled layout ldmatrix reads without bank conflicts; page ids are
+//     fetched 32 at a time by the whole warp.
 //   consumers: each warp takes every 4th page and runs, per page of 16 keys,
 //     S^T = K Q^T  (mma.sync m16n8k16: 16 keys x 8 query rows, K from smem via
 //     ldmatrix, Q^T held in registers), online softmax per query column in
 //     the log2 domain, P^T moved to the B-fragment layout with movmatrix, and
 //     O^T += V^T P^T (ldmatrix.trans).  Query rows >= GRP are zero padding.
-//   merge: the 4 warps' (O, m, l) are merged in shared memory; a unit with one
-//     CTA writes its output directly, otherwise every CTA writes its partial to
-//     the workspace and the last CTA to finish (atomic ticket -- no waiting)
-//     combines them with the log-sum-exp rule.  The finishing CTA then writes
-//     the new token's K/V into its page slot (attend, then append).
+//   merge: the 4 warps' (O, m, l) are merged in shared memory.  A unit with one
+//     CTA writes its output directly.  A unit with several CTAs is split in
+//     multiples of 8, launched as thread-block clusters of 8: the 8 CTAs of a
+//     cluster merge their partials through distributed shared memory (each
+//     CTA reduces 1/8 of the outputs), one partial per cluster goes to the
+//     workspace, and the last cluster of the unit to finish (atomic ticket --
+//     nothing waits on another cluster) combines the unit's partials with the
+//     log-sum-exp rule, again spread over its 8 CTAs.  The finishing CTA then
+//     writes the new token's K/V into its page slot (attend, then append).
 #include <cfloat>
 
 #include "common.cuh"
 #include "internal.h"
+#include "page_layout.cuh"
 
 namespace aoh {
 namespace {
@@ -48,11 +55,13 @@ constexpr int kPartialFloats = kMaxGrp * kHeadDim + 2 * kMaxGrp;
 constexpr int kOPitch = kHeadDim + 4;  // padded row of the warp-merge scratch
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
 constexpr int kCounterBytes = kMaxUnits * 4;
+constexpr int kCluster = 8;
 
 struct DecodePlan {
   int n_units;
+  int total_ctas;                // CTAs with work; the grid is padded to a multiple of kCluster
   int unit[kMaxUnits];           // ((b * G + g) << 1) | is_retrieval
-  int cta_begin[kMaxUnits + 1];  // prefix sum of splits
+  int cta_begin[kMaxUnits + 1];  // prefix sum of splits; units with > 1 split are cluster-aligned
 };
 
 struct DecodeArgs {
@@ -128,8 +137,7 @@ __device__ __forceinline__ int append_slot(const UnitView& uv, int pos, int* j) 
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    decode_bf16_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a,
-                       const DecodePlan plan) {
+    decode_bf16_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodePlan plan) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   __shared__ __align__(8) uint64_t full_bar[kStages];
@@ -137,12 +145,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_bad[kStages];
   __shared__ float s_m[kConsumerWarps][kMaxGrp];
   __shared__ float s_l[kConsumerWarps][kMaxGrp];
-  __shared__ int s_last;
-  __shared__ int s_abort;
+  __shared__ volatile int s_last;
+  __shared__ volatile int s_abort;
+  __shared__ float cp_o[kMaxGrp][kHeadDim];  // this CTA's merged partial (read by its cluster)
+  __shared__ float cp_m[kMaxGrp], cp_l[kMaxGrp];
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bid = blockIdx.x;
+  if (bid >= plan.total_ctas) return;  // cluster padding (only in clusters that never synchronise)
 
   // ---- which unit / split is this CTA ----
   int lo = 0, hi = plan.n_units;
@@ -189,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ===================== producer =====================
     int issued = 0;
-    if (lane == 0) prefetch_tmap(&tmap);
+    const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
     int nxt = -1;
     if (lane < nloc) nxt = bt[uv.table_index(v0 + lane)];
     for (int base = 0; base < nloc; base += 32) {
@@ -207,8 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (pid >= 0 && pid < G.num_pages) {
             s_bad[st] = 0;
             mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
-            tma_load_4d(smem + st * kStageBytes, &tmap, &full_bar[st], 0, 0, 0, pid);
-            tma_load_4d(smem + st * kStageBytes + kStageBytes / 2, &tmap, &full_bar[st], 64, 0, 0, pid);
+            bulk_load(smem + st * kStageBytes, pool + (size_t)pid * kPageBf16Bytes, kStageBytes, &full_bar[st]);
             issued = i + 1;
           } else {
             atomicOr(G.err, kErrBadPage);
@@ -251,6 +261,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int vj = v0 + i;
       int p0 = uv.key_pos(vj, t0), p1 = uv.key_pos(vj, t0 + 8);
       if (s_bad[st]) p0 = p1 = -1;
+      // Slots that hold no attended key (tail of the last page, ring slots not
+      // yet written, keys outside the window) get probability 0, but their V
+      // rows may hold any bit pattern and 0 * NaN = NaN inside the MMA: zero them.
+      const uint32_t ok_lo = __ballot_sync(0xffffffffu, p0 >= 0);
+      const uint32_t ok_hi = __ballot_sync(0xffffffffu, p1 >= 0);
+      const bool partial = (ok_lo & ok_hi) != 0xffffffffu;
+      if (partial) {
+        uint8_t* stage = smem + st * kStageBytes;
+        for (int c = lane; c < kPage * 2 * 8; c += 32) {  // (slot, half, 16-byte chunk)
+          const int slot = c >> 4, half = (c >> 3) & 1, chunk = c & 7;
+          const uint32_t okm = slot < 8 ? ok_lo : ok_hi;
+          if (!((okm >> ((slot & 7) * 4)) & 1u))
+            *reinterpret_cast<uint4*>(stage + half * (kStageBytes / 2) + 2048 + slot * 128 + chunk * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+      }
 
       // ---- S^T (16 keys x 8 query rows) = K Q^T ----
       float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -308,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      if (partial) fence_proxy_async_smem();  // generic writes before the next TMA fill of this stage
       if (lane == 0) mbar_arrive(&empty_bar[st]);
     }
 
@@ -383,7 +411,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   __nv_bfloat16* out_u = a.out + ((size_t)b * G.Hq + (size_t)g * grp) * kHeadDim;
-  float* part = a.ws + (size_t)bid * kPartialFloats;
   for (int e = tid; e < grp * kHeadDim; e += kThreads) {
     const int qq = e >> 7, d = e & (kHeadDim - 1);
     float M = -INFINITY;
@@ -400,61 +427,79 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (nsplit == 1) {
       out_u[e] = __float2bfloat16(acc / L);
     } else {
-      part[qq * kHeadDim + d] = acc;
+      cp_o[qq][d] = acc;
       if (d == 0) {
-        part[kMaxGrp * kHeadDim + qq] = M;
-        part[kMaxGrp * kHeadDim + kMaxGrp + qq] = L;
+        cp_m[qq] = M;
+        cp_l[qq] = L;
       }
     }
   }
 
   if (nsplit > 1) {
-    // ===================== split combine: the last CTA of the unit =====================
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int ticket = atomicAdd(&a.counters[u], 1);
-      s_last = ticket == nsplit - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float* parts = a.ws + (size_t)plan.cta_begin[u] * kPartialFloats;
-    float* sw = reinterpret_cast<float*>(smem);  // [split][kMaxGrp] weights
-    // weights w_s = exp2(m_s - M) / L, one warp per query row
-    for (int qq = warp; qq < grp; qq += kThreads / 32) {
-      float M = -INFINITY;
-      for (int s = lane; s < nsplit; s += 32)
-        M = fmaxf(M, __ldcg(parts + (size_t)s * kPartialFloats + kMaxGrp * kHeadDim + qq));
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      const float Mu = M == -INFINITY ? 0.f : M;
-      float L = 0.f;
-      for (int s = lane; s < nsplit; s += 32) {
-        const float* ps = parts + (size_t)s * kPartialFloats + kMaxGrp * kHeadDim;
-        const float f = fast_exp2(__ldcg(ps + qq) - Mu);
-        sw[s * kMaxGrp + qq] = f;
-        L += __ldcg(ps + kMaxGrp + qq) * f;
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      const float inv = 1.f / L;
-      __syncwarp();
-      for (int s = lane; s < nsplit; s += 32) sw[s * kMaxGrp + qq] *= inv;
-    }
-    __syncthreads();
-    for (int e = tid; e < grp * kHeadDim; e += kThreads) {
+    // ============ cluster merge: 8 consecutive splits -> one partial (DSMEM) ============
+    // nsplit is a multiple of kCluster and the unit's first CTA is cluster-aligned,
+    // so this cluster holds splits [split - rank, split - rank + 8) of this unit only.
+    cluster_sync_all();
+    const int rank = (int)cluster_ctarank();
+    const int E = grp * kHeadDim;
+    const int slice = (E + kCluster - 1) / kCluster;  // outputs reduced by this CTA
+    const int e_lo = rank * slice, e_hi = min(E, e_lo + slice);
+    const int nk = nsplit / kCluster;                 // partials of the unit
+    const int kidx = split / kCluster;
+    float* parts = a.ws + (size_t)(plan.cta_begin[u] / kCluster) * kPartialFloats;
+    for (int e = e_lo + tid; e < e_hi; e += kThreads) {
       const int qq = e >> 7, d = e & (kHeadDim - 1);
-      float acc0 = 0.f, acc1 = 0.f;
-      int s = 0;
-      for (; s + 1 < nsplit; s += 2) {
-        acc0 += __ldcg(parts + (size_t)s * kPartialFloats + qq * kHeadDim + d) * sw[s * kMaxGrp + qq];
-        acc1 += __ldcg(parts + (size_t)(s + 1) * kPartialFloats + qq * kHeadDim + d) *
-                sw[(s + 1) * kMaxGrp + qq];
+      float mc[kCluster];
+      float M = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kCluster; ++c) {
+        mc[c] = ld_dsmem_f32(mapa_shared(&cp_m[qq], c));
+        M = fmaxf(M, mc[c]);
       }
-      if (s < nsplit) acc0 += __ldcg(parts + (size_t)s * kPartialFloats + qq * kHeadDim + d) * sw[s * kMaxGrp + qq];
-      out_u[e] = __float2bfloat16(acc0 + acc1);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float acc = 0.f, L = 0.f;
+#pragma unroll
+      for (int c = 0; c < kCluster; ++c) {
+        const float f = fast_exp2(mc[c] - Mu);
+        acc += ld_dsmem_f32(mapa_shared(&cp_o[qq][d], c)) * f;
+        L += ld_dsmem_f32(mapa_shared(&cp_l[qq], c)) * f;
+      }
+      float* pk = parts + (size_t)kidx * kPartialFloats;
+      pk[qq * kHeadDim + d] = acc;
+      if (d == 0) {
+        pk[kMaxGrp * kHeadDim + qq] = M;
+        pk[kMaxGrp * kHeadDim + kMaxGrp + qq] = L;
+      }
     }
+    __threadfence();
+    cluster_sync_all();  // the cluster's partial is complete; no DSMEM reads after this
+    if (rank == 0 && tid == 0) {
+      const int ticket = atomicAdd(&a.counters[u], 1);
+      const uint32_t last = ticket == nk - 1;
+      for (int c = 0; c < kCluster; ++c) st_dsmem_u32(mapa_shared((const void*)&s_last, c), last);
+    }
+    cluster_sync_all();
+    if (!s_last) return;
+    // ============ last cluster of the unit: combine its nk partials, 1/8 of outputs per CTA ============
+    __threadfence();
+    for (int e = e_lo + tid; e < e_hi; e += kThreads) {
+      const int qq = e >> 7, d = e & (kHeadDim - 1);
+      float M = -INFINITY;
+#pragma unroll 8
+      for (int k = 0; k < nk; ++k)
+        M = fmaxf(M, __ldcg(parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + qq));
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float acc = 0.f, L = 0.f;
+#pragma unroll 8
+      for (int k = 0; k < nk; ++k) {
+        const float* pk = parts + (size_t)k * kPartialFloats;
+        const float f = fast_exp2(__ldcg(pk + kMaxGrp * kHeadDim + qq) - Mu);
+        acc += __ldcg(pk + qq * kHeadDim + d) * f;
+        L += __ldcg(pk + kMaxGrp * kHeadDim + kMaxGrp + qq) * f;
+      }
+      out_u[e] = __float2bfloat16(acc / L);
+    }
+    if (rank != 0) return;
     if (tid == 0) a.counters[u] = 0;  // ready for the next launch
   }
 
@@ -467,33 +512,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pid < 0 || pid >= G.num_pages) {
         if (tid == 0) atomicOr(G.err, kErrBadPage);
       } else {
-        const int kv = tid >> 4, part16 = tid & 15;  // 16 lanes x 16 B per row
+        const int kv = tid >> 4, c8 = tid & 15;  // 16 lanes x 16 B per row
         const __nv_bfloat16* src = (kv ? a.v_new : a.k_new) + ((size_t)b * G.G + g) * kHeadDim;
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(G.pool) +
-                             (size_t)pid * (2 * kPage * kHeadDim) + ((size_t)kv * kPage + slot) * kHeadDim;
-        reinterpret_cast<uint4*>(dst)[part16] = reinterpret_cast<const uint4*>(src)[part16];
+        uint8_t* dst = static_cast<uint8_t*>(G.pool) + (size_t)pid * kPageBf16Bytes + bf16_chunk_offset(kv, slot, c8);
+        *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(src)[c8];
       }
     }
   }
 }
 
-int g_occupancy = 0;
+int g_max_ctas = 0;  // CTAs resident at once when launched in clusters of kCluster
+
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kDynSmem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
 
 int ensure_kernel_attrs(int device) {
   static int configured_device = -1;
-  if (configured_device == device && g_occupancy > 0) return AOH_OK;
+  if (configured_device == device && g_max_ctas > 0) return AOH_OK;
   int rc = cuda_check(cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            kDynSmem),
                       "decode: set smem attribute");
   if (rc) return rc;
-  int occ = 0;
-  rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_bf16_kernel, kThreads, kDynSmem),
-                  "decode: occupancy");
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr);
+  int clusters = 0;
+  rc = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel, &cfg), "decode: cluster occupancy");
   if (rc) return rc;
-  if (occ <= 0) return fail(AOH_ERR_CUDA, "decode kernel cannot be resident on an SM");
-  g_occupancy = occ;
+  if (clusters <= 0) return fail(AOH_ERR_CUDA, "decode kernel clusters cannot be resident");
+  g_max_ctas = std::min(kMaxCtas, clusters * kCluster);
   configured_device = device;
   return AOH_OK;
+}
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Splits of a unit with `pages` units of work at `per` pages per CTA: 1, or a
+// multiple of the cluster size.
+int splits_for(int64_t pages, int64_t per) {
+  const int64_t n = std::max<int64_t>(1, (pages + per - 1) / per);
+  if (n == 1) return 1;
+  return (int)std::min<int64_t>(kMaxSplit, round_up((int)std::min<int64_t>(n, kMaxSplit), kCluster));
 }
 
 }  // namespace
@@ -508,7 +578,6 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   const int grp = cf.num_q_heads / cf.num_kv_heads;
   if (grp > kMaxGrp)
     return fail(AOH_ERR_UNSUPPORTED, "decode: query heads per KV head (%d) above %d", grp, kMaxGrp);
-  if (!c->tmap_ok) return fail(AOH_ERR_STATE, "decode: pool tensor map missing (cache not bound?)");
   if (ws_bytes < decode_workspace_bytes(c) || !ws)
     return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace of %zu bytes is smaller than %zu", ws_bytes,
                 decode_workspace_bytes(c));
@@ -517,9 +586,9 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   int rc = ensure_kernel_attrs(c->device);
   if (rc) return rc;
 
-  // ---- plan: units of this layer stored here, split so that one wave fills the GPU ----
-  DecodePlan plan;
-  int pages[kMaxUnits];
+  // ---- plan: the units of this layer stored here, split so one wave fills the GPU ----
+  int code[kMaxUnits];
+  int64_t pages[kMaxUnits];
   int n = 0;
   int64_t total = 0;
   const int T = past_len;
@@ -533,31 +602,38 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
       if (!c->owned[uidx]) continue;
       if (n >= kMaxUnits) return fail(AOH_ERR_UNSUPPORTED, "decode: more than %d units in a layer", kMaxUnits);
       const bool r = c->retrieval(layer, g);
-      if (r && c->unit_npages[uidx] * kPage < T + 1)
-        return fail(AOH_ERR_OUT_OF_PAGES, "decode: positions up to %d not reserved (layer %d seq %d head %d)",
-                    T, layer, b, g);
-      plan.unit[n] = ((b * cf.num_kv_heads + g) << 1) | (r ? 1 : 0);
-      pages[n] = (r ? ret_pages : stream_pages) + 1;
+      code[n] = ((b * cf.num_kv_heads + g) << 1) | (r ? 1 : 0);
+      pages[n] = (r ? ret_pages : stream_pages) + 1;  // + the new key
       total += pages[n];
       ++n;
     }
   if (n == 0) return AOH_OK;
-  plan.n_units = n;
-  const int target = std::min(kMaxCtas, c->num_sms * g_occupancy);
+  const int target = g_max_ctas;
   int64_t per = std::max<int64_t>(4, (total + target - 1) / target);
-  int ctas = 0;
+  int grid = 0;
   for (;;) {
-    ctas = 0;
-    for (int i = 0; i < n; ++i)
-      ctas += (int)std::min<int64_t>(kMaxSplit, std::max<int64_t>(1, (pages[i] + per - 1) / per));
-    if (ctas <= target || ctas <= n) break;
+    int ctas = 0;
+    for (int i = 0; i < n; ++i) ctas += splits_for(pages[i], per);
+    grid = round_up(ctas, kCluster);
+    if (grid <= target || per > total) break;
     per = per + per / 16 + 1;
   }
-  if (ctas > kMaxCtas) return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d CTAs", ctas);
-  plan.cta_begin[0] = 0;
-  for (int i = 0; i < n; ++i)
-    plan.cta_begin[i + 1] =
-        plan.cta_begin[i] + (int)std::min<int64_t>(kMaxSplit, std::max<int64_t>(1, (pages[i] + per - 1) / per));
+  if (grid > kMaxCtas) return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d CTAs", grid);
+  // units split across clusters first (cluster-aligned), single-CTA units after
+  DecodePlan plan;
+  plan.n_units = n;
+  int k = 0, begin = 0;
+  for (int pass = 0; pass < 2; ++pass)
+    for (int i = 0; i < n; ++i) {
+      const int sp = splits_for(pages[i], per);
+      if ((sp > 1) != (pass == 0)) continue;
+      plan.unit[k] = code[i];
+      plan.cta_begin[k] = begin;
+      begin += sp;
+      ++k;
+    }
+  plan.cta_begin[n] = begin;
+  plan.total_ctas = begin;
 
   DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -570,57 +646,9 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
   a.counters = static_cast<int*>(ws);
   a.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
-  decode_bf16_kernel<<<ctas, kThreads, kDynSmem, st>>>(c->tmap_pool, a, plan);
-  return cuda_check(cudaGetLastError(), "decode kernel launch");
-}
-
-// ---------------------------------------------------------------------------
-// TMA descriptor of the bf16 pool: dims (dim 128, slot 16, kv 2, page P),
-// box (64, 16, 2, 1) with 128-byte swizzle: one box = one 64-dim half of a
-// page's K and V (4 KB).
-// ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult qr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
-        qr == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
-                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = get_encode_fn();
-  if (!fn) return fail(AOH_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t d[5], s[4];
-  cuuint32_t bx[5], es[5];
-  for (int i = 0; i < rank; ++i) {
-    d[i] = dims[i];
-    bx[i] = box[i];
-    es[i] = 1;
-    if (i + 1 < rank) s[i] = strides_bytes[i];
-  }
-  CUresult r = fn(map, dt, (cuuint32_t)rank, base, d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(AOH_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return AOH_OK;
-}
-
-int encode_pool_tmap(aoh_kv_cache* c) {
-  const uint64_t dims[4] = {(uint64_t)kHeadDim, (uint64_t)kPage, 2, (uint64_t)c->cfg.num_pages};
-  const uint64_t strides[3] = {kHeadDim * 2, kPage * kHeadDim * 2, 2 * kPage * kHeadDim * 2};
-  const uint32_t box[4] = {64, (uint32_t)kPage, 2, 1};
-  int rc = encode_tiled(&c->tmap_pool, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, c->pool, dims, strides, box,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-  c->tmap_ok = rc == AOH_OK;
-  return rc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_config(grid, st, attr);
+  return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");
 }
 
 }  // namespace aoh

@@ -57,8 +57,6 @@ struct aoh_kv_cache {
   bool bound = false;
   int device = -1;
   int num_sms = 0;
-  CUtensorMap tmap_pool;  // bf16 pool, 128B-swizzled 64-column boxes
-  bool tmap_ok = false;
 
   int unit(int layer, int b, int g) const { return (layer * cfg.batch + b) * cfg.num_kv_heads + g; }
   bool retrieval(int layer, int g) const { return labels[layer * cfg.num_kv_heads + g] != 0; }
@@ -74,5 +72,4 @@ int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, con
                         const void* k_new, const void* v_new, void* out, cudaStream_t st);
 int launch_append(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* k_new,
                   const void* v_new, cudaStream_t st);
-int encode_pool_tmap(aoh_kv_cache* c);
 }  // namespace aoh

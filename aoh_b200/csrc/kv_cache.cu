@@ -212,10 +212,6 @@ int aoh_kv_bind(aoh_kv_cache* c, void* pool, void* tables, aoh_stream stream) {
   c->dirty_hi = (int64_t)c->table.size();
   rc = aoh_kv_sync(c, stream);
   if (rc) return rc;
-  if (c->cfg.dtype == AOH_BF16 && c->cfg.num_pages > 0) {
-    rc = encode_pool_tmap(c);
-    if (rc) return rc;
-  }
   // host mirror must stay alive until the async copies ran
   return cuda_check(cudaStreamSynchronize(st), "aoh_kv_bind sync");
 }
@@ -313,37 +309,31 @@ int aoh_kv_unit_pages(const aoh_kv_cache* c, int32_t layer, int32_t seq, int32_t
   return AOH_OK;
 }
 
-int64_t aoh_kv_row_offset(const aoh_kv_cache* c, int32_t layer, int32_t seq, int32_t kv_head,
-                          int32_t position, int32_t past_len, int32_t is_value) {
-  if (!c) return -1;
+int aoh_kv_locate(const aoh_kv_cache* c, int32_t layer, int32_t seq, int32_t kv_head, int32_t position,
+                  int32_t past_len, int32_t* page, int32_t* slot) {
+  if (!c || !page || !slot) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_locate: null argument");
+  *page = *slot = -1;
   const auto& cf = c->cfg;
   if (layer < 0 || layer >= cf.num_layers || seq < 0 || seq >= cf.batch || kv_head < 0 ||
-      kv_head >= cf.num_kv_heads || position < 0)
-    return -1;
-  int u = c->unit(layer, seq, kv_head);
-  if (!c->owned[u]) return -1;
-  int64_t j, slot;
-  if (c->retrieval(layer, kv_head)) {
-    if (position >= past_len) return -1;
+      kv_head >= cf.num_kv_heads || position < 0 || past_len < 0)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_locate: index out of range");
+  const int u = c->unit(layer, seq, kv_head);
+  if (!c->owned[u] || position >= past_len) return AOH_OK;
+  int64_t j, s;
+  if (c->retrieval(layer, kv_head) || position < cf.sink_size) {
     j = position / kPage;
-    slot = position % kPage;
+    s = position % kPage;
   } else {
-    // stored iff inside the sink, or among the latest ring_cap positions
-    if (position >= past_len) return -1;
-    if (position < cf.sink_size) {
-      j = position / kPage;
-      slot = position % kPage;
-    } else {
-      if (c->ring_cap == 0 || position < past_len - c->ring_cap) return -1;
-      int64_t r = (position - cf.sink_size) % c->ring_cap;
-      j = c->sink_pages + r / kPage;
-      slot = r % kPage;
-    }
+    // a streaming head keeps positions >= sink only among the latest ring_cap
+    if (c->ring_cap == 0 || position < past_len - c->ring_cap) return AOH_OK;
+    const int64_t r = (position - cf.sink_size) % c->ring_cap;
+    j = c->sink_pages + r / kPage;
+    s = r % kPage;
   }
-  if (j >= c->unit_npages[u]) return -1;
-  int32_t page = c->table[c->unit_offset[u] + j];
-  if (page < 0) return -1;
-  return (int64_t)page * c->page_bytes + ((int64_t)is_value * kPage + slot) * kHeadDim * c->elem_bytes;
+  if (j >= c->unit_npages[u]) return AOH_OK;
+  *page = c->table[c->unit_offset[u] + j];
+  *slot = *page >= 0 ? (int32_t)s : -1;
+  return AOH_OK;
 }
 
 int aoh_kv_device_status(aoh_kv_cache* c, int32_t* flags, aoh_stream stream) {

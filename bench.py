@@ -463,6 +463,13 @@ def classifier_check(torch, dev):
     return res
 
 
+def _set_workload(context: int, layers: int) -> None:
+    global T_CTX, L_LAYERS, WORKLOAD
+    if context != T_CTX or layers != L_LAYERS:
+        T_CTX, L_LAYERS = context, layers
+        WORKLOAD = f"llama31_8b_decode_{T_CTX}_ctx_{L_LAYERS}_layers"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -473,7 +480,10 @@ def main():
     ap.add_argument("--cpu-calls", type=int, default=10)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-classifier", action="store_true")
+    ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
+    ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
     args = ap.parse_args()
+    _set_workload(args.context, args.layers)
     if args.warmup < 3 and args.impl == "aoh":
         print("note: --warmup raised to 3", file=sys.stderr)
         args.warmup = 3

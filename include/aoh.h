@@ -119,10 +119,16 @@ AOH_API int32_t aoh_kv_free_pages(const aoh_kv_cache* cache);
 AOH_API int aoh_kv_unit_pages(const aoh_kv_cache* cache, int32_t layer, int32_t seq, int32_t kv_head,
                       int32_t* pages, int32_t capacity, int32_t* n_pages);
 
-/* Device byte offset of `position` of unit (layer, seq, kv_head) inside the
- * pool for the K row (is_value = 0) or V row (1); -1 if not stored. */
-AOH_API int64_t aoh_kv_row_offset(const aoh_kv_cache* cache, int32_t layer, int32_t seq, int32_t kv_head,
-                          int32_t position, int32_t past_len, int32_t is_value);
+/* Where `position` of unit (layer, seq, kv_head) is stored, given past_len
+ * cached tokens: *page (pool page id) and *slot (0..15), both -1 if the
+ * position is not held (evicted from a streaming head, not yet cached, or the
+ * unit is not stored here).  Page layout in the pool:
+ *   f32 (16 KB):  row-major [kv: 0 = K, 1 = V][slot: 16][dim: 128];
+ *   bf16 (8 KB):  [half h: dims 64h..64h+63][kv][slot][128 bytes], the 16-byte
+ *                 chunk c of a row stored at chunk c ^ (slot & 7) -- the 128-byte
+ *                 swizzle the tensor-core kernels read directly. */
+AOH_API int aoh_kv_locate(const aoh_kv_cache* cache, int32_t layer, int32_t seq, int32_t kv_head,
+                          int32_t position, int32_t past_len, int32_t* page, int32_t* slot);
 
 /* Read and clear the device-side check word (bounds checks, bounded waits);
  * synchronizes `stream`. *flags == 0 means no check tripped. */

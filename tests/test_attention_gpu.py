@@ -99,7 +99,7 @@ def test_long_context_decode_against_oracle(cuda_device, T):
     q = torch.randn((B, 1, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
     kn = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
     vn = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
-    cache = AoHKVCache(labels, Hq, batch=B, max_context=T + 1, dtype=torch.bfloat16)
+    cache = AoHKVCache(labels, Hq, batch=B, max_context=T + 2, dtype=torch.bfloat16)
     _fill_cache_bf16(cache, 0, k_ctx, v_ctx)
     out = aoh_attention(cache, 0, q, kn, vn)
     got = out.float().cpu().numpy()
@@ -152,3 +152,30 @@ def test_bad_arguments_raise(cuda_device):
     cache.kv_seq_len = 64
     with pytest.raises(torch.OutOfMemoryError):
         aoh_attention(cache, 0, q, kv, kv)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_append_layout_roundtrip(cuda_device, dtype):
+    """aoh_kv_append writes rows where aoh_kv_locate says they are, in the
+    documented page layout (pre-swizzled for bf16), for both head kinds."""
+    labels = np.array([[1, 0]], dtype=np.float64)
+    sink, recent, T = 20, 40, 137
+    cache = AoHKVCache(labels, 4, batch=2, sink_size=sink, recent_size=recent, max_context=T, dtype=dtype)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    k = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(dtype)
+    v = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(dtype)
+    for s in range(0, T, 50):
+        e = min(T, s + 50)
+        cache.kv_seq_len = s
+        cache.append_layer(0, k[:, s:e].contiguous(), v[:, s:e].contiguous())
+    cache.kv_seq_len = T
+    for seq in range(2):
+        ret_pos = list(range(T))
+        kk, vv = cache.read_rows(0, seq, 0, ret_pos)
+        assert torch.equal(kk, k[seq, :, 0]) and torch.equal(vv, v[seq, :, 0])
+        ring = (recent + 15) // 16 * 16
+        str_pos = list(range(sink)) + list(range(T - ring, T))
+        kk, vv = cache.read_rows(0, seq, 1, str_pos)
+        assert torch.equal(kk, k[seq, str_pos, 1]) and torch.equal(vv, v[seq, str_pos, 1])
+        assert cache.locate(0, seq, 1, sink + 1) == (-1, -1)  # evicted
+    assert cache.device_status() == 0

@@ -83,19 +83,20 @@ def test_paging_reserve_release_and_row_offsets():
     assert L.aoh_kv_unit_pages(h, 0, 1, 0, buf, 16, C.byref(n)) == 0 and n.value == 3
     pages = list(buf[:3])
     assert len(set(pages)) == 3
-    # retrieval row offset: position 17 -> page 1, slot 1
-    page_bytes = 2 * 16 * 128 * 2
-    off = L.aoh_kv_row_offset(h, 0, 1, 0, 17, 33, 0)
-    assert off == pages[1] * page_bytes + 1 * 128 * 2
-    assert L.aoh_kv_row_offset(h, 0, 1, 0, 17, 33, 1) == off + 16 * 128 * 2
-    assert L.aoh_kv_row_offset(h, 0, 1, 0, 40, 33, 0) == -1  # not yet cached
+    def locate(layer, seq, g, pos, past):
+        pg, sl = C.c_int32(), C.c_int32()
+        assert L.aoh_kv_locate(h, layer, seq, g, pos, past, C.byref(pg), C.byref(sl)) == 0
+        return pg.value, sl.value
+    # retrieval: position 17 -> page 1, slot 1
+    assert locate(0, 1, 0, 17, 33) == (pages[1], 1)
+    assert locate(0, 1, 0, 40, 33) == (-1, -1)  # not yet cached
     # streaming ring: sink 20 -> positions < 20 in sink pages; position 95 of a 96-token context
     assert L.aoh_kv_unit_pages(h, 0, 0, 1, buf, 16, C.byref(n)) == 0 and n.value == str_pages
     sp = list(buf[:str_pages])
     r = (95 - 20) % 48
-    assert L.aoh_kv_row_offset(h, 0, 0, 1, 95, 96, 0) == sp[2 + r // 16] * page_bytes + (r % 16) * 256
-    assert L.aoh_kv_row_offset(h, 0, 0, 1, 19, 96, 0) == sp[1] * page_bytes + 3 * 256
-    assert L.aoh_kv_row_offset(h, 0, 0, 1, 30, 96, 0) == -1  # evicted (older than the ring)
+    assert locate(0, 0, 1, 95, 96) == (sp[2 + r // 16], r % 16)
+    assert locate(0, 0, 1, 19, 96) == (sp[1], 3)
+    assert locate(0, 0, 1, 30, 96) == (-1, -1)  # evicted (older than the ring)
     # exceeding max_context and exhausting the pool
     assert L.aoh_kv_reserve(h, -1, 101) == _lib.OUT_OF_PAGES
     assert L.aoh_kv_release(h, 1) == 0
