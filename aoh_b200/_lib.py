@@ -18,6 +18,7 @@ ABI_VERSION = 1
 
 OK, INVALID, OUT_OF_PAGES, CUDA, UNSUPPORTED, STATE, DEVICE_CHECK = range(7)
 F32, BF16 = 0, 1
+PAST_LEN_DEVICE = -1
 
 
 class KVConfig(C.Structure):
@@ -56,6 +57,8 @@ _SIGNATURES = {
     "aoh_kv_locate": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(_i32), C.POINTER(_i32)]),
     "aoh_kv_device_status": (C.c_int, [_vp, C.POINTER(_i32), _vp]),
     "aoh_decode_workspace_bytes": (C.c_size_t, [_vp]),
+    "aoh_kv_set_length": (C.c_int, [_vp, _i32, _vp]),
+    "aoh_kv_advance": (C.c_int, [_vp, _i32, _vp]),
     "aoh_attn_decode": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, C.c_size_t, _vp]),
     "aoh_attn_prefill": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "aoh_kv_append": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp]),

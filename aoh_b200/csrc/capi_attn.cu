@@ -43,12 +43,17 @@ size_t aoh_decode_workspace_bytes(const aoh_kv_cache* c) { return c ? decode_wor
 
 int aoh_attn_decode(aoh_kv_cache* c, int32_t layer, int32_t past_len, const void* q, const void* k_new,
                     const void* v_new, void* out, void* workspace, size_t workspace_bytes, aoh_stream stream) {
-  int rc = check_common(c, layer, past_len, 1, q, k_new, v_new, out, "aoh_attn_decode");
+  const bool dev_len = past_len == AOH_PAST_LEN_DEVICE;
+  if (dev_len && c && c->cfg.dtype != AOH_BF16)
+    return fail(AOH_ERR_UNSUPPORTED, "aoh_attn_decode: device-resident length needs a bf16 cache");
+  const int32_t plan_len = dev_len ? (c ? c->len_hint : 0) : past_len;
+  int rc = check_common(c, layer, plan_len, 1, q, k_new, v_new, out, "aoh_attn_decode");
   if (rc) return rc;
   if (!q || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_decode: null q/out");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (c->cfg.dtype == AOH_BF16)
-    return launch_decode_bf16(c, layer, past_len, q, k_new, v_new, out, workspace, workspace_bytes, st);
+    return launch_decode_bf16(c, layer, plan_len, q, k_new, v_new, out, workspace, workspace_bytes, st,
+                              dev_len ? c->dev_err + 1 : nullptr);
   rc = launch_attn_generic(c, layer, past_len, 1, q, k_new, v_new, out, st);
   if (rc) return rc;
   return launch_append(c, layer, past_len, 1, k_new, v_new, st);

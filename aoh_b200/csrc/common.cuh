@@ -100,6 +100,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 // ----------------------------------------------------------------------------
+// programmatic dependent launch
+// ----------------------------------------------------------------------------
+// Wait until the preceding kernel in the stream has completed and its memory
+// is visible (no-op when launched without a programmatic dependency).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to begin launching.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------
 // thread-block clusters (distributed shared memory)
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {

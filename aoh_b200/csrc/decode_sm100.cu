@@ -72,6 +72,7 @@ struct DecodeArgs {
   CacheGeom geom;
   int layer;
   int T;             // past_len: cached positions are [0, T), the query is at T
+  const int* T_dev;  // if non-null, past_len is read from here (CUDA-graph replay)
   float scale_log2;  // D^-0.5 * log2(e)
   float* ws;         // partials, kMaxCtas x kPartialFloats
   int* counters;     // kMaxUnits tickets, zero between launches
@@ -97,6 +98,15 @@ struct UnitView {
   }
   __device__ __forceinline__ int n_pages() const {
     return retr ? (T + kPage - 1) / kPage : sp_used + rp_used;
+  }
+  // Compact index of the page holding position T - 1 (the token the previous
+  // decode step appended), or -1.
+  __device__ __forceinline__ int last_written_page() const {
+    const int p = T - 1;
+    if (p < 0) return -1;
+    if (retr || p < sink) return p / kPage;
+    if (ring_cap == 0) return -1;
+    return sp_used + ((p - sink) % ring_cap) / kPage;
   }
   __device__ __forceinline__ int table_index(int vj) const {
     return retr ? vj : (vj < sp_used ? vj : sink_pages + (vj - sp_used));
@@ -170,8 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nsplit = plan.cta_begin[u + 1] - plan.cta_begin[u];
   const int grp = G.grp;
 
+  // The length is only written by the advance kernel, which never overlaps a
+  // decode kernel (it does not trigger its dependents early).
+  const int T = a.T_dev ? *a.T_dev : a.T;
   UnitView uv;
-  uv.init(retr, a.T, G);
+  uv.init(retr, T, G);
   const int npg = uv.n_pages();
   const int per = (npg + nsplit - 1) / nsplit;
   const int v0 = min(npg, split * per);
@@ -201,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ===================== producer =====================
     int issued = 0;
     const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
+    const int hot_vj = uv.last_written_page();
     int nxt = -1;
     if (lane < nloc) nxt = bt[uv.table_index(v0 + lane)];
     for (int base = 0; base < nloc; base += 32) {
@@ -209,6 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cnt = min(32, nloc - base);
       for (int k = 0; k < cnt; ++k) {
         const int pid = __shfl_sync(0xffffffffu, my, k);
+        // This page may still be receiving the previous kernel's append (when it
+        // decoded the same layer): wait for that kernel before loading it.
+        if (v0 + base + k == hot_vj) griddep_wait();
         if (lane == 0 && !s_abort) {
           const int i = base + k, st = i % kStages, rnd = i / kStages;
           bool ok = true;
@@ -235,9 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = max(0, issued - kStages); i < issued; ++i)
         mbar_wait(&full_bar[i % kStages], (i / kStages) & 1, G.err);
     }
+    griddep_wait();  // before this warp's share of the output / workspace writes
   } else {
     // ===================== consumers =====================
     const int cw = warp - 1;
+    // q, k_new, v_new may be produced by the previous kernel in the stream and
+    // the workspace is shared with it: wait for it here (the producer has
+    // already started streaming this layer's pages, which it does not write).
+    griddep_wait();
+    if (tid == 32) griddep_launch_dependents();
     // Q^T B-fragments: qf[kk][0] = Q[n][16kk+2c..+1], qf[kk][1] = Q[n][16kk+8+2c..+1], n = lane/4
     uint32_t qf[8][2];
     {
@@ -482,22 +505,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!s_last) return;
     // ============ last cluster of the unit: combine its nk partials, 1/8 of outputs per CTA ============
     __threadfence();
-    for (int e = e_lo + tid; e < e_hi; e += kThreads) {
-      const int qq = e >> 7, d = e & (kHeadDim - 1);
+    // weights w[k][q] = exp2(m_k - M_q) / L_q in shared memory (the stage ring is free)
+    float* sw = reinterpret_cast<float*>(smem);      // [nk][kMaxGrp]
+    float* sml = sw + kMaxSplit / kCluster * kMaxGrp;  // [nk][kMaxGrp][2] raw (m, l)
+    for (int i = tid; i < nk * grp; i += kThreads) {
+      const int k = i / grp, qq = i % grp;
+      const float* pk = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim;
+      sml[(k * kMaxGrp + qq) * 2] = __ldcg(pk + qq);
+      sml[(k * kMaxGrp + qq) * 2 + 1] = __ldcg(pk + kMaxGrp + qq);
+    }
+    __syncthreads();
+    for (int qq = warp; qq < grp; qq += kThreads / 32) {
       float M = -INFINITY;
-#pragma unroll 8
-      for (int k = 0; k < nk; ++k)
-        M = fmaxf(M, __ldcg(parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + qq));
+      for (int k = lane; k < nk; k += 32) M = fmaxf(M, sml[(k * kMaxGrp + qq) * 2]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
       const float Mu = M == -INFINITY ? 0.f : M;
-      float acc = 0.f, L = 0.f;
-#pragma unroll 8
-      for (int k = 0; k < nk; ++k) {
-        const float* pk = parts + (size_t)k * kPartialFloats;
-        const float f = fast_exp2(__ldcg(pk + kMaxGrp * kHeadDim + qq) - Mu);
-        acc += __ldcg(pk + qq * kHeadDim + d) * f;
-        L += __ldcg(pk + kMaxGrp * kHeadDim + kMaxGrp + qq) * f;
+      float L = 0.f;
+      for (int k = lane; k < nk; k += 32) {
+        const float f = fast_exp2(sml[(k * kMaxGrp + qq) * 2] - Mu);
+        sw[k * kMaxGrp + qq] = f;
+        L += sml[(k * kMaxGrp + qq) * 2 + 1] * f;
       }
-      out_u[e] = __float2bfloat16(acc / L);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      const float inv = 1.f / L;
+      __syncwarp();
+      for (int k = lane; k < nk; k += 32) sw[k * kMaxGrp + qq] *= inv;
+    }
+    __syncthreads();
+    for (int e = e_lo + tid; e < e_hi; e += kThreads) {
+      const int qq = e >> 7;
+      const float* po = parts + e;  // partial k's output e at po[k * kPartialFloats]
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      int k = 0;
+      for (; k + 16 <= nk; k += 16) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __ldcg(po + (size_t)(k + j) * kPartialFloats);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j & 3] += v[j] * sw[(k + j) * kMaxGrp + qq];
+      }
+      for (; k < nk; ++k) acc[0] += __ldcg(po + (size_t)k * kPartialFloats) * sw[k * kMaxGrp + qq];
+      out_u[e] = __float2bfloat16((acc[0] + acc[1]) + (acc[2] + acc[3]));
     }
     if (rank != 0) return;
     if (tid == 0) a.counters[u] = 0;  // ready for the next launch
@@ -506,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ===================== append the new token (after every read of the unit) =====================
   if (tid < 32) {
     int j = 0;
-    const int slot = append_slot(uv, a.T, &j);
+    const int slot = append_slot(uv, T, &j);
     if (slot >= 0) {
       const int pid = bt[j];
       if (pid < 0 || pid >= G.num_pages) {
@@ -523,7 +573,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int g_max_ctas = 0;  // CTAs resident at once when launched in clusters of kCluster
 
-cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr) {
+// attr must have room for 2 attributes: cluster shape and programmatic
+// stream serialization (the kernel may start while the previous kernel in the
+// stream finishes; it synchronises with griddepcontrol.wait).
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -533,8 +586,10 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
   attr[0].val.clusterDim.x = kCluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cfg;
 }
 
@@ -545,8 +600,8 @@ int ensure_kernel_attrs(int device) {
                                            kDynSmem),
                       "decode: set smem attribute");
   if (rc) return rc;
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr);
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr, false);
   int clusters = 0;
   rc = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel, &cfg), "decode: cluster occupancy");
   if (rc) return rc;
@@ -573,7 +628,8 @@ size_t decode_workspace_bytes(const aoh_kv_cache*) {
 }
 
 int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
-                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,
+                       const int* past_len_dev) {
   const auto& cf = c->cfg;
   const int grp = cf.num_q_heads / cf.num_kv_heads;
   if (grp > kMaxGrp)
@@ -643,11 +699,12 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   a.geom = c->geom();
   a.layer = layer;
   a.T = T;
+  a.T_dev = past_len_dev;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
   a.counters = static_cast<int*>(ws);
   a.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = launch_config(grid, st, attr);
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config(grid, st, attr, true);
   return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");
 }
 

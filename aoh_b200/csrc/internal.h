@@ -53,7 +53,8 @@ struct aoh_kv_cache {
   int32_t* dev_base = nullptr;  // tables buffer
   int32_t* dev_unit_offset = nullptr;
   int32_t* dev_table = nullptr;
-  int32_t* dev_err = nullptr;
+  int32_t* dev_err = nullptr;   // [0] check word, [1] device-resident sequence length
+  int32_t len_hint = 0;          // host copy of the device length (plans kernels in device mode)
   bool bound = false;
   int device = -1;
   int num_sms = 0;
@@ -66,7 +67,9 @@ struct aoh_kv_cache {
 namespace aoh {
 // launchers (return aoh_status)
 int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
-                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st);
+                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,
+                       const int* past_len_dev);
+int launch_set_length(aoh_kv_cache* c, int value, int add, cudaStream_t st);
 size_t decode_workspace_bytes(const aoh_kv_cache* c);
 int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q,
                         const void* k_new, const void* v_new, void* out, cudaStream_t st);

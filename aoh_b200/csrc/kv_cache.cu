@@ -67,6 +67,19 @@ aoh::CacheGeom aoh_kv_cache::geom() const {
   return g;
 }
 
+namespace aoh {
+
+__global__ void set_length_kernel(int32_t* len, int value, int add) {
+  if (add) *len += value; else *len = value;
+}
+
+int launch_set_length(aoh_kv_cache* c, int value, int add, cudaStream_t st) {
+  set_length_kernel<<<1, 1, 0, st>>>(c->dev_err + 1, value, add);
+  return cuda_check(cudaGetLastError(), "length kernel launch");
+}
+
+}  // namespace aoh
+
 extern "C" {
 
 int aoh_abi_version(void) { return AOH_ABI_VERSION; }
@@ -289,6 +302,25 @@ int aoh_kv_sync(aoh_kv_cache* c, aoh_stream stream) {
   // host mirror may change right after; keep ordering simple and safe.
   rc = cuda_check(cudaStreamSynchronize(st), "aoh_kv_sync");
   c->dirty_lo = c->dirty_hi = 0;
+  return rc;
+}
+
+int aoh_kv_set_length(aoh_kv_cache* c, int32_t length, aoh_stream stream) {
+  if (!c) return fail(AOH_ERR_INVALID_ARGUMENT, "null cache");
+  if (!c->bound) return fail(AOH_ERR_STATE, "cache is not bound to device memory");
+  if (length < 0 || length > c->cfg.max_context)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "length %d outside [0, max_context]", length);
+  int rc = launch_set_length(c, length, 0, static_cast<cudaStream_t>(stream));
+  if (rc == AOH_OK) c->len_hint = length;
+  return rc;
+}
+
+int aoh_kv_advance(aoh_kv_cache* c, int32_t n, aoh_stream stream) {
+  if (!c) return fail(AOH_ERR_INVALID_ARGUMENT, "null cache");
+  if (!c->bound) return fail(AOH_ERR_STATE, "cache is not bound to device memory");
+  if (n < 0) return fail(AOH_ERR_INVALID_ARGUMENT, "n must be non-negative");
+  int rc = launch_set_length(c, n, 1, static_cast<cudaStream_t>(stream));
+  if (rc == AOH_OK) c->len_hint += n;
   return rc;
 }
 

@@ -1,0 +1,81 @@
+"""A decode step through every layer, captured once as a CUDA graph.
+
+The reference runs decode as an eager Python loop over layers
+(eval/efficiency/benchmark_llama31.py:319-338); each layer's attention here is
+one kernel launch, so on the host side a step is only launch overhead.
+``DecodeStepGraph`` captures the whole step -- one decode kernel per layer,
+then one tiny kernel that advances the device-resident sequence length (the
+reference's ``kv_seq_len += q_len`` after the last layer, :249-250) -- and
+replays it.  Consecutive layer kernels are launched with programmatic
+dependent launch, so a layer's page streaming starts while the previous
+layer's kernel finishes.
+
+Inputs and outputs are the fixed tensors given at construction; write a
+step's q/k/v into them before ``replay()`` (or let producing kernels do so).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .cache import AoHKVCache
+
+
+class DecodeStepGraph:
+    """Decode step over ``layers`` of ``cache`` as one CUDA graph.
+
+    q: (L, B, 1, Hq, D), k/v: (L, B, 1, G, D), out: (L, B, 1, Hq, D) -- bf16,
+    contiguous, on the cache's device, L = number of layers in the step.
+    ``max_steps``: replays this graph will be used for (pages are reserved
+    for all of them up front; the graph itself never allocates).
+    """
+
+    def __init__(self, cache: AoHKVCache, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 out: torch.Tensor, max_steps: int, layers=None):
+        if cache.dtype != torch.bfloat16:
+            raise ValueError("graph decode needs a bfloat16 cache")
+        self.cache = cache
+        self.layers = list(range(cache.num_layers)) if layers is None else list(layers)
+        if q.shape[0] != len(self.layers):
+            raise ValueError("q/k/v/out must have one leading entry per captured layer")
+        for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+            if not t.is_contiguous() or t.dtype != torch.bfloat16 or t.device != cache.device:
+                raise ValueError(f"{name} must be a contiguous bf16 tensor on {cache.device}")
+        self.q, self.k, self.v, self.out = q, k, v, out
+        cache.reserve(cache.kv_seq_len + max_steps + 1)
+        self._L = cache._L
+        self._ws = cache.decode_workspace()
+        self._set_length(cache.kv_seq_len)
+        # the first launch configures kernel attributes (not capturable): run the
+        # step once eagerly with the length not advanced -- it appends at the
+        # current position, which the first replay rewrites with the same data
+        self._launch_layers()
+        torch.cuda.synchronize(cache.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._launch_layers()
+            _lib.check(self._L.aoh_kv_advance(cache._h, 1, C.c_void_p(_lib.stream_handle())),
+                       "aoh_kv_advance")
+        # capture does not execute: put the device length back to the host's
+        self._set_length(cache.kv_seq_len)
+
+    def _set_length(self, n: int) -> None:
+        _lib.check(self._L.aoh_kv_set_length(self.cache._h, n, C.c_void_p(_lib.stream_handle())),
+                   "aoh_kv_set_length")
+
+    def _launch_layers(self) -> None:
+        st = C.c_void_p(_lib.stream_handle())
+        h = self.cache._h
+        for i, layer in enumerate(self.layers):
+            rc = self._L.aoh_attn_decode(h, layer, _lib.PAST_LEN_DEVICE, C.c_void_p(self.q[i].data_ptr()),
+                                         C.c_void_p(self.k[i].data_ptr()), C.c_void_p(self.v[i].data_ptr()),
+                                         C.c_void_p(self.out[i].data_ptr()), C.c_void_p(self._ws.data_ptr()),
+                                         self._ws.numel(), st)
+            _lib.check(rc, "aoh_attn_decode")
+
+    def replay(self) -> None:
+        """Run one decode step (all captured layers) and advance the length."""
+        self.graph.replay()
+        self.cache.kv_seq_len += 1

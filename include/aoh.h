@@ -145,13 +145,25 @@ AOH_API int aoh_kv_device_status(aoh_kv_cache* cache, int32_t* flags, aoh_stream
 /* Positions [0, past_len + q_len) must be reserved (aoh_kv_reserve + sync). */
 /* ------------------------------------------------------------------------- */
 
+/* Device-resident sequence length, for decode steps replayed from a CUDA
+ * graph: aoh_kv_set_length writes it, aoh_kv_advance adds to it (one tiny
+ * kernel each, stream-ordered, capturable), and aoh_attn_decode reads it when
+ * called with past_len = AOH_PAST_LEN_DEVICE.  The host keeps a copy of the
+ * expected value to size kernel launches; pages for every length the device
+ * will reach must be reserved and synced beforehand. */
+#define AOH_PAST_LEN_DEVICE (-1)
+AOH_API int aoh_kv_set_length(aoh_kv_cache* cache, int32_t length, aoh_stream stream);
+AOH_API int aoh_kv_advance(aoh_kv_cache* cache, int32_t n, aoh_stream stream);
+
 /* Upper bound of the workspace aoh_attn_decode needs (bytes). */
 AOH_API size_t aoh_decode_workspace_bytes(const aoh_kv_cache* cache);
 
 /* Decode step (q_len = 1): split-KV over the paged cache, combine, append.
- * workspace: caller-owned device memory of aoh_decode_workspace_bytes(),
- * zero-filled once before its first use; calls sharing a workspace must not
- * overlap on the GPU. */
+ * past_len may be AOH_PAST_LEN_DEVICE (bf16 caches).  workspace: caller-owned
+ * device memory of aoh_decode_workspace_bytes(), zero-filled once before its
+ * first use; calls sharing a workspace must be ordered on one stream (the
+ * kernel starts early under programmatic dependent launch and waits for the
+ * previous kernel before touching q, outputs or the workspace). */
 AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len, const void* q,
                     const void* k_new, const void* v_new, void* out, void* workspace,
                     size_t workspace_bytes, aoh_stream stream);
