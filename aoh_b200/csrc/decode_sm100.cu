@@ -74,7 +74,7 @@ struct DecodeArgs {
   int T;             // past_len: cached positions are [0, T), the query is at T
   const int* T_dev;  // if non-null, past_len is read from here (CUDA-graph replay)
   float scale_log2;  // D^-0.5 * log2(e)
-  float* ws;         // partials, kMaxCtas x kPartialFloats
+  float* ws;         // per-cluster partials, (kMaxCtas / kCluster) x kPartialFloats
   int* counters;     // kMaxUnits tickets, zero between launches
 };
 
@@ -623,8 +623,10 @@ int splits_for(int64_t pages, int64_t per) {
 
 }  // namespace
 
+// Workspace: one ticket per unit of a launch, then one partial (O, m, l) per
+// cluster -- at most kMaxCtas / kCluster of them.
 size_t decode_workspace_bytes(const aoh_kv_cache*) {
-  return (size_t)kCounterBytes + (size_t)kMaxCtas * kPartialFloats * sizeof(float);
+  return (size_t)kCounterBytes + (size_t)(kMaxCtas / kCluster) * kPartialFloats * sizeof(float);
 }
 
 int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
