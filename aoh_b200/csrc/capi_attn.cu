@@ -5,8 +5,8 @@
 
 using namespace aoh;
 
-static int check_common(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q_len, const void* q,
-                        const void* k_new, const void* v_new, const void* out, const char* who) {
+int aoh::check_common(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q_len, const void* q,
+                      const void* k_new, const void* v_new, const void* out, const char* who) {
   if (!c) return fail(AOH_ERR_INVALID_ARGUMENT, "%s: null cache", who);
   if (!c->bound) return fail(AOH_ERR_STATE, "%s: cache is not bound to device memory", who);
   if (layer < 0 || layer >= c->cfg.num_layers)

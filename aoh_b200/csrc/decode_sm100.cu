@@ -629,18 +629,14 @@ size_t decode_workspace_bytes(const aoh_kv_cache*) {
   return (size_t)kCounterBytes + (size_t)(kMaxCtas / kCluster) * kPartialFloats * sizeof(float);
 }
 
-int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
-                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,
-                       const int* past_len_dev) {
+// Plan the layer's split over at most `max_clusters` cluster partials and launch.
+static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
+                    const void* v_new, void* out, void* ws, int max_clusters, cudaStream_t st,
+                    const int* past_len_dev) {
   const auto& cf = c->cfg;
   const int grp = cf.num_q_heads / cf.num_kv_heads;
   if (grp > kMaxGrp)
     return fail(AOH_ERR_UNSUPPORTED, "decode: query heads per KV head (%d) above %d", grp, kMaxGrp);
-  if (ws_bytes < decode_workspace_bytes(c) || !ws)
-    return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace of %zu bytes is smaller than %zu", ws_bytes,
-                decode_workspace_bytes(c));
-  if (reinterpret_cast<uintptr_t>(ws) % 16)
-    return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace must be 16-byte aligned");
   int rc = ensure_kernel_attrs(c->device);
   if (rc) return rc;
 
@@ -666,7 +662,7 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
       ++n;
     }
   if (n == 0) return AOH_OK;
-  const int target = g_max_ctas;
+  const int target = std::min(g_max_ctas, max_clusters * kCluster);
   int64_t per = std::max<int64_t>(4, (total + target - 1) / target);
   int grid = 0;
   for (;;) {
@@ -677,6 +673,9 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
     per = per + per / 16 + 1;
   }
   if (grid > kMaxCtas) return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d CTAs", grid);
+  if (grid / kCluster > max_clusters)
+    return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d cluster partials, the workspace holds %d",
+                grid / kCluster, max_clusters);
   // units split across clusters first (cluster-aligned), single-CTA units after
   DecodePlan plan;
   plan.n_units = n;
@@ -708,6 +707,17 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(grid, st, attr, true);
   return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");
+}
+
+int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
+                       const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,
+                       const int* past_len_dev) {
+  if (ws_bytes < decode_workspace_bytes(c) || !ws)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace of %zu bytes is smaller than %zu", ws_bytes,
+                decode_workspace_bytes(c));
+  if (reinterpret_cast<uintptr_t>(ws) % 16)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace must be 16-byte aligned");
+  return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, ws, kMaxCtas / kCluster, st, past_len_dev);
 }
 
 }  // namespace aoh

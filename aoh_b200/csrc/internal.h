@@ -65,6 +65,9 @@ struct aoh_kv_cache {
 };
 
 namespace aoh {
+// Validation shared by the attention entry points (aoh_status).
+int check_common(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q_len, const void* q,
+                 const void* k_new, const void* v_new, const void* out, const char* who);
 // launchers (return aoh_status)
 int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
                        const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,

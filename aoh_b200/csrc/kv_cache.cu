@@ -26,15 +26,14 @@
 
 namespace aoh {
 
-static thread_local std::string g_last_error;
+// Fixed per-thread buffer: reporting an error never allocates.
+static thread_local char g_last_error[1024];
 
 int fail(int code, const char* fmt, ...) {
-  char buf[1024];
   va_list ap;
   va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
   va_end(ap);
-  g_last_error = buf;
   return code;
 }
 
@@ -84,7 +83,7 @@ extern "C" {
 
 int aoh_abi_version(void) { return AOH_ABI_VERSION; }
 
-const char* aoh_last_error(void) { return g_last_error.c_str(); }
+const char* aoh_last_error(void) { return g_last_error; }
 
 int aoh_kv_create(const aoh_kv_config* cfg, aoh_kv_cache** out) {
   if (!cfg || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_create: null argument");
