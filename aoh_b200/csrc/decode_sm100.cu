@@ -35,6 +35,7 @@
 //     log-sum-exp rule, again spread over its 8 CTAs.  The finishing CTA then
 //     writes the new token's K/V into its page slot (attend, then append).
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -720,4 +721,73 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
   return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, ws, kMaxCtas / kCluster, st, past_len_dev);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode: aoh_attn_decode_noalloc.
+//
+// For callers that cannot allocate device memory (see include/aoh.h), the
+// decode workspace lives in a file-scope device array instead of a
+// caller-provided buffer.  It holds the per-unit tickets and up to
+// kNoAllocClusters cluster partials: 1 KB + 64 x 4160 B = 267,264 bytes, which
+// every GPU that loads this library keeps until the process exits.  The array
+// is shared by every call: calls that overlap on the GPU race on it.
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocClusters = 64;
+constexpr size_t kNoAllocScratchBytes =
+    (size_t)kCounterBytes + (size_t)kNoAllocClusters * kPartialFloats * sizeof(float);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+
+// Once per device, with that device current: the array's device address (the
+// host-side name is only a stand-in) and zeroed tickets.  Stream-ordered on
+// `st`, so this first call must not be inside a stream capture.
+int noalloc_scratch(int device, cudaStream_t st, void** out) {
+  if (device < 0 || device >= kMaxDevices) return fail(AOH_ERR_UNSUPPORTED, "device ordinal %d", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    int rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "no-alloc decode: scratch address");
+    if (rc) return rc;
+    rc = cuda_check(cudaMemsetAsync(p, 0, kCounterBytes, st), "no-alloc decode: clear tickets");
+    if (rc) return rc;
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return AOH_OK;
+}
+}  // namespace
+
 }  // namespace aoh
+
+extern "C" int aoh_attn_decode_noalloc(aoh_kv_cache* c, int32_t layer, int32_t past_len, const void* q,
+                                       const void* k_new, const void* v_new, void* out, aoh_stream stream) {
+  using namespace aoh;
+  if (c && c->cfg.dtype != AOH_BF16)
+    return fail(AOH_ERR_UNSUPPORTED, "aoh_attn_decode_noalloc: bf16 caches only");
+  int rc = check_common(c, layer, past_len, 1, q, k_new, v_new, out, "aoh_attn_decode_noalloc");
+  if (rc) return rc;
+  if (!q || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_decode_noalloc: null q/out");
+  int n_units = 0;
+  for (int b = 0; b < c->cfg.batch; ++b)
+    for (int g = 0; g < c->cfg.num_kv_heads; ++g) n_units += c->owned[c->unit(layer, b, g)] ? 1 : 0;
+  if (n_units > kMaxUnits)
+    return fail(AOH_ERR_UNSUPPORTED,
+                "aoh_attn_decode_noalloc: %d (sequence, KV head) units in layer %d; the static scratch "
+                "holds tickets for at most %d",
+                n_units, layer, kMaxUnits);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = -1;
+  rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev != c->device)
+    return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_decode_noalloc: current device %d, cache on %d", dev,
+                c->device);
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, st, &scratch);
+  if (rc) return rc;
+  // plan_and_launch rejects a plan needing more than kNoAllocClusters partials
+  return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, scratch, kNoAllocClusters, st, nullptr);
+}

@@ -168,6 +168,27 @@ AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len
                     const void* k_new, const void* v_new, void* out, void* workspace,
                     size_t workspace_bytes, aoh_stream stream);
 
+/* aoh_attn_decode without a workspace argument, for callers that cannot
+ * allocate device memory: plugin hosts that hand an op only its input and
+ * output buffers and own every allocation themselves, and runtimes that may
+ * not allocate after start-up (fixed memory budgets, allocators that are not
+ * reachable from the calling layer).  No counterpart in the reference, whose
+ * eager path allocates new tensors on every call.
+ *
+ * The split-KV scratch is a static device array inside libaoh.so: 267,264
+ * bytes (tickets for 256 units + 64 cluster partials), held on every GPU that
+ * loads the library until the process exits.  bf16 caches only; a layer whose
+ * plan would need more than 256 (sequence, KV head) units or more than 64
+ * cluster partials is rejected with AOH_ERR_UNSUPPORTED (a one-wave plan on a
+ * 148-SM B200 needs at most 45).  The first call on a device looks up the
+ * array's device address and zeroes its tickets on `stream` -- make that first
+ * call outside any stream capture.  Every call shares the array and it keeps
+ * the last call's contents: calls that overlap on the GPU (two streams, two
+ * caches at once) race; order them on one stream.  Allocates nothing: no
+ * cudaMalloc, no cudaFree, no allocating library routine. */
+AOH_API int aoh_attn_decode_noalloc(aoh_kv_cache* cache, int32_t layer, int32_t past_len, const void* q,
+                                    const void* k_new, const void* v_new, void* out, aoh_stream stream);
+
 /* Prefill chunk (any q_len >= 1): causal attention for retrieval heads,
  * sink + window for streaming heads, then append. */
 AOH_API int aoh_attn_prefill(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,
