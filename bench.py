@@ -308,13 +308,13 @@ def run_aoh(args):
     bytes_launch = decode_layer_bytes(T_mid, n_ret_units, n_str_units, B)
     launch_us = ms * 1000.0 / L_LAYERS
     achieved = bytes_launch / (launch_us * 1e-6) / 1e9
+    # DRAM bytes per launch from the committed ncu summary (64K capture scaled to 128K)
     traffic = None
-    tp = ROOT / "profiles" / "decode_bf16_128k_traffic.json"
-    if tp.exists():
-        try:
-            traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
-        except ValueError:
-            traffic = None
+    tp = ROOT / "profiles" / "decode_bf16_64k_ncu_full.md"
+    if tp.exists() and T_CTX == 131072:
+        import re
+        m = re.search(r"dram_bytes_per_launch_128k = (\d+)", tp.read_text())
+        traffic = int(m.group(1)) if m else None
 
     # ---------------- end to end through the public API, host buffers ----------------
     e2e = None
