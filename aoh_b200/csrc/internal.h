@@ -74,6 +74,8 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
                        const int* past_len_dev);
 int launch_set_length(aoh_kv_cache* c, int value, int add, cudaStream_t st);
 size_t decode_workspace_bytes(const aoh_kv_cache* c);
+int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
+                        const void* v_new, void* out, cudaStream_t st);
 int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q,
                         const void* k_new, const void* v_new, void* out, cudaStream_t st);
 int launch_append(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* k_new,

@@ -215,7 +215,7 @@ def run_aoh(args):
                                             T_CTX, SINK, RECENT, world,
                                             owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
     owned = (owner == rank).astype(np.uint8)
-    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 8
+    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 4096
     cache = AoHKVCache(labels, HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
                        dtype=torch.bfloat16, device=dev, owned=owned, reserve_all=True)
     gen = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
@@ -273,15 +273,19 @@ def run_aoh(args):
             dist.barrier()
 
     # ---------------- device-timed region ----------------
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    torch.cuda.synchronize()
-    T0 = cache.kv_seq_len
     props = torch.cuda.get_device_properties(dev)
     uuid = str(getattr(props, "uuid", "") or "")
     clocks = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or local))
-    clocks.start()
+    clocks.start()  # sampling runs through warm-up and the timed steps (the same steady load)
+    for _ in range(args.warmup):
+        step()
+    t_w = time.perf_counter()
+    while not clocks.lines and time.perf_counter() - t_w < 2.0:  # until nvidia-smi reports under load
+        step()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    T0 = cache.kv_seq_len
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     h0 = time.perf_counter()
@@ -491,8 +495,8 @@ def _set_workload(context: int, layers: int) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["aoh", "reference"], default="aoh")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-calls", type=int, default=10)
