@@ -19,7 +19,9 @@
 // inside the window, so evicted or out-of-window keys are never loaded.
 //
 // Warp roles (192 threads):
-//   warp 0   producer: Q once, then K/V tiles into a 2-stage ring (mbarriers).
+//   warp 0   producer: Q once, then K and V tiles into two 3-stage rings
+//            (mbarriers); K of a tile is released as soon as its QK^T is
+//            done, so loads run ahead of the PV that still needs V.
 //   warp 1   allocates 512 TMEM columns; lane 0 issues every tcgen05.mma:
 //              S[j%2] = Q K_j^T  (SS: both operands in shared memory, K-major)
 //              O     += P_{j-1} V_{j-1}  (TS: P from TMEM, V MN-major)
@@ -44,9 +46,9 @@ constexpr int BN = 128;  // keys per tile
 constexpr int kPThreads = 192;
 constexpr int kQBytes = 2 * BM * 128;       // [half][row][128 B]
 constexpr int kKVHalf = BN * 128;           // one 64-dim half of K or V for a tile
-constexpr int kStageBytesP = 4 * kKVHalf;   // [K lo][K hi][V lo][V hi]
-constexpr int kPStages = 2;
-constexpr int kPSmem = kQBytes + kPStages * kStageBytesP + 1024;
+constexpr int kTileBytes = 2 * kKVHalf;     // K (or V) of one tile: [half][key][128 B]
+constexpr int kPStages = 3;                 // separate K and V rings of 3 tiles each
+constexpr int kPSmem = kQBytes + 2 * kPStages * kTileBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 __device__ __forceinline__ uint32_t col_s(int s) { return s ? 128u : 0u; }    // S0 / S1
@@ -170,9 +172,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024p(smem_raw);
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + kQBytes;
+  uint8_t* sK = smem + kQBytes;                    // K ring: stage s at sK + s * kTileBytes
+  uint8_t* sV = sK + kPStages * kTileBytes;        // V ring
   __shared__ __align__(8) uint64_t bar_q, bar_final;
-  __shared__ __align__(8) uint64_t bar_kv_full[kPStages], bar_kv_empty[kPStages];
+  __shared__ __align__(8) uint64_t bar_k_full[kPStages], bar_k_empty[kPStages];
+  __shared__ __align__(8) uint64_t bar_v_full[kPStages], bar_v_empty[kPStages];
   __shared__ __align__(8) uint64_t bar_s_full[2], bar_s_free[2], bar_p_full[2], bar_o_done[2];
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
@@ -196,8 +200,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     mbar_init(&bar_q, 1);
     mbar_init(&bar_final, 1);
     for (int s = 0; s < kPStages; ++s) {
-      mbar_init(&bar_kv_full[s], 1);
-      mbar_init(&bar_kv_empty[s], 1);
+      mbar_init(&bar_k_full[s], 1);
+      mbar_init(&bar_k_empty[s], 1);
+      mbar_init(&bar_v_full[s], 1);
+      mbar_init(&bar_v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_s_full[s], 1);
@@ -210,8 +216,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
   // Tile regions never loaded (tail of the last cache tile) must hold finite
   // values: P is 0 there, but 0 * NaN would poison the MMA.
-  for (int i = tid; i < kPStages * kStageBytesP / 16; i += kPThreads)
-    reinterpret_cast<uint4*>(sKV)[i] = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < 2 * kPStages * kTileBytes / 16; i += kPThreads)
+    reinterpret_cast<uint4*>(sK)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -238,9 +244,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int ids = ids_next;
       ids_next = fetch_ids(j + 1);  // page ids of the next tile, in flight during this one
       const int s = j % kPStages, rnd = j / kPStages;
-      uint8_t* st = sKV + s * kStageBytesP;
+      uint8_t* kst = sK + s * kTileBytes;
+      uint8_t* vst = sV + s * kTileBytes;
       if (lane == 0 && rnd > 0 && !s_abort) {
-        if (!mbar_wait(&bar_kv_empty[s], (rnd - 1) & 1, G.err)) s_abort = 1;
+        if (!mbar_wait(&bar_k_empty[s], (rnd - 1) & 1, G.err)) s_abort = 1;
+        if (!s_abort && !mbar_wait(&bar_v_empty[s], (rnd - 1) & 1, G.err)) s_abort = 1;
       }
       __syncwarp();
       if (s_abort) break;
@@ -251,29 +259,32 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint32_t okm = __ballot_sync(0xffffffffu, lane < 8 && ok);
         if (lane == 0) {
           if (okm == 0) {
-            mbar_arrive(&bar_kv_full[s]);
+            mbar_arrive(&bar_k_full[s]);
+            mbar_arrive(&bar_v_full[s]);
           } else {
-            mbar_arrive_expect_tx(&bar_kv_full[s], __popc(okm) * kPageBf16Bytes);
+            mbar_arrive_expect_tx(&bar_k_full[s], __popc(okm) * (kPageBf16Bytes / 2));
+            mbar_arrive_expect_tx(&bar_v_full[s], __popc(okm) * (kPageBf16Bytes / 2));
           }
         }
         __syncwarp();
-        // lane jp < 8 copies page jp's four 2 KB blocks into the four tile halves
+        // lane jp < 8 copies page jp's four 2 KB blocks into the K and V tile halves
         if (lane < 8 && ok) {
           const uint8_t* src = pool + (size_t)ids * kPageBf16Bytes;
           const int row_off = lane * kPage * 128;
-          bulk_load(st + 0 * kKVHalf + row_off, src + 0 * kBlockBytes, kBlockBytes, &bar_kv_full[s]);  // K lo
-          bulk_load(st + 2 * kKVHalf + row_off, src + 1 * kBlockBytes, kBlockBytes, &bar_kv_full[s]);  // V lo
-          bulk_load(st + 1 * kKVHalf + row_off, src + 2 * kBlockBytes, kBlockBytes, &bar_kv_full[s]);  // K hi
-          bulk_load(st + 3 * kKVHalf + row_off, src + 3 * kBlockBytes, kBlockBytes, &bar_kv_full[s]);  // V hi
+          bulk_load(kst + 0 * kKVHalf + row_off, src + 0 * kBlockBytes, kBlockBytes, &bar_k_full[s]);  // K lo
+          bulk_load(kst + 1 * kKVHalf + row_off, src + 2 * kBlockBytes, kBlockBytes, &bar_k_full[s]);  // K hi
+          bulk_load(vst + 0 * kKVHalf + row_off, src + 1 * kBlockBytes, kBlockBytes, &bar_v_full[s]);  // V lo
+          bulk_load(vst + 1 * kKVHalf + row_off, src + 3 * kBlockBytes, kBlockBytes, &bar_v_full[s]);  // V hi
         }
       } else if (lane == 0) {
         int r0, lo, hi;
         tl.chunk(j, &r0, &lo, &hi);
-        mbar_arrive_expect_tx(&bar_kv_full[s], kStageBytesP);
-        tma_load_4d(st + 0 * kKVHalf, &tm_k, &bar_kv_full[s], 0, g, r0, b);
-        tma_load_4d(st + 1 * kKVHalf, &tm_k, &bar_kv_full[s], 64, g, r0, b);
-        tma_load_4d(st + 2 * kKVHalf, &tm_v, &bar_kv_full[s], 0, g, r0, b);
-        tma_load_4d(st + 3 * kKVHalf, &tm_v, &bar_kv_full[s], 64, g, r0, b);
+        mbar_arrive_expect_tx(&bar_k_full[s], kTileBytes);
+        tma_load_4d(kst + 0 * kKVHalf, &tm_k, &bar_k_full[s], 0, g, r0, b);
+        tma_load_4d(kst + 1 * kKVHalf, &tm_k, &bar_k_full[s], 64, g, r0, b);
+        mbar_arrive_expect_tx(&bar_v_full[s], kTileBytes);
+        tma_load_4d(vst + 0 * kKVHalf, &tm_v, &bar_v_full[s], 0, g, r0, b);
+        tma_load_4d(vst + 1 * kKVHalf, &tm_v, &bar_v_full[s], 64, g, r0, b);
       }
       issued = j + 1;
       __syncwarp();
@@ -281,8 +292,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // nothing this CTA issued may still be landing when it exits
     if (lane == 0) {
       mbar_wait(&bar_q, 0, G.err);
-      for (int j = max(0, issued - kPStages); j < issued; ++j)
-        mbar_wait(&bar_kv_full[j % kPStages], (j / kPStages) & 1, G.err);
+      for (int j = max(0, issued - kPStages); j < issued; ++j) {
+        mbar_wait(&bar_k_full[j % kPStages], (j / kPStages) & 1, G.err);
+        mbar_wait(&bar_v_full[j % kPStages], (j / kPStages) & 1, G.err);
+      }
     }
   } else if (warp == 1) {
     // ============================ MMA issuer ============================
@@ -294,27 +307,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_after();
       auto pv = [&](int t) {
         const int s = t & 1;
-        if (!mbar_wait(&bar_p_full[s], (t >> 1) & 1, G.err)) {
+        if (!mbar_wait(&bar_v_full[t % kPStages], (t / kPStages) & 1, G.err) ||
+            !mbar_wait(&bar_p_full[s], (t >> 1) & 1, G.err)) {
           s_abort = 1;
           return false;
         }
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sKV + (t % kPStages) * kStageBytesP + 2 * kKVHalf);
+        const uint32_t v_addr = smem_u32(sV + (t % kPStages) * kTileBytes);
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
           const uint64_t vdesc = smem_desc_sw128(v_addr + k * 16 * 128, kKVHalf, 1024);
           mma_ts(tmem + kColO, tmem + col_p(s) + 8 * k, vdesc, kIdescPV, (t > 0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&bar_o_done[s]);
-        mma_commit(&bar_kv_empty[t % kPStages]);
+        mma_commit(&bar_v_empty[t % kPStages]);
         return true;
       };
       for (int j = 0; j < n_tiles && ok && !s_abort; ++j) {
         const int s = j & 1;
-        if (!mbar_wait(&bar_kv_full[j % kPStages], (j / kPStages) & 1, G.err)) break;
+        if (!mbar_wait(&bar_k_full[j % kPStages], (j / kPStages) & 1, G.err)) break;
         if (j >= 2 && !mbar_wait(&bar_s_free[s], ((j >> 1) - 1) & 1, G.err)) break;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + (j % kPStages) * kStageBytesP);
+        const uint32_t k_addr = smem_u32(sK + (j % kPStages) * kTileBytes);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * kKVHalf + (k & 3) * 32;
@@ -323,6 +337,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           mma_ss(tmem + col_s(s), adesc, bdesc, kIdescQK, k > 0 ? 1u : 0u);
         }
         mma_commit(&bar_s_full[s]);
+        mma_commit(&bar_k_empty[j % kPStages]);
         if (j >= 1 && !pv(j - 1)) break;
       }
       if (n_tiles > 0 && !s_abort) pv(n_tiles - 1);

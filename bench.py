@@ -502,6 +502,7 @@ def main():
     ap.add_argument("--cpu-calls", type=int, default=10)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-classifier", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
     ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
     ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
     args = ap.parse_args()
@@ -511,6 +512,12 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.prefill_only:
+        import torch
+        torch.cuda.set_device(0)
+        _, bf16_peak, _ = measured_peaks()
+        print(json.dumps({"prefill": prefill_sample(torch, torch.device("cuda", 0), bf16_peak)}), flush=True)
+        return 0
     return run_aoh(args)
 
 
