@@ -135,7 +135,9 @@ class AoHKVCache:
         1024-token steps, capped at max_context)."""
         if n_tokens <= self._reserved:
             return
-        target = min(self.max_context, max(n_tokens, self._reserved + 1024))
+        # whole 128-token runs keep 8 consecutive page ids per key tile (the
+        # prefill kernel then fetches a tile with 4 TMA loads instead of 32 copies)
+        target = min(self.max_context, -(-max(n_tokens, self._reserved + 1024) // 128) * 128)
         _lib.check(self._L.aoh_kv_reserve(self._h, -1, target), "AoHKVCache.reserve")
         _lib.check(self._L.aoh_kv_sync(self._h, C.c_void_p(_lib.stream_handle())))
         self._reserved = target

@@ -58,6 +58,10 @@ struct aoh_kv_cache {
   bool bound = false;
   int device = -1;
   int num_sms = 0;
+  // bf16 pool viewed as (64 elems, 16 slots, kv, half, page): one box of 8
+  // consecutive pages gathers one (kv, half) block of each into a 128-key tile
+  CUtensorMap tmap_pool_runs;
+  bool tmap_pool_runs_ok = false;
 
   int unit(int layer, int b, int g) const { return (layer * cfg.batch + b) * cfg.num_kv_heads + g; }
   bool retrieval(int layer, int g) const { return labels[layer * cfg.num_kv_heads + g] != 0; }

@@ -21,7 +21,10 @@
 // Warp roles (192 threads):
 //   warp 0   producer: Q once, then K and V tiles into two 3-stage rings
 //            (mbarriers); K of a tile is released as soon as its QK^T is
-//            done, so loads run ahead of the PV that still needs V.
+//            done, so loads run ahead of the PV that still needs V.  A cache
+//            tile whose 8 pages have consecutive ids (the allocator hands out
+//            runs) is fetched with 4 TMA tensor loads over the pool; other
+//            tiles with one 2 KB bulk copy per (page, K|V, half).
 //   warp 1   allocates 512 TMEM columns; lane 0 issues every tcgen05.mma:
 //              S[j%2] = Q K_j^T  (SS: both operands in shared memory, K-major)
 //              O     += P_{j-1} V_{j-1}  (TS: P from TMEM, V MN-major)
@@ -168,7 +171,8 @@ __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
 
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ PrefillArgs a) {
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_pool,
+                        const __grid_constant__ PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024p(smem_raw);
   uint8_t* sQ = smem;
@@ -257,6 +261,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const bool want = lane < 8 && j * 8 + lane < tl.n_pages;
         if (want && !ok) atomicOr(G.err, kErrBadPage);
         const uint32_t okm = __ballot_sync(0xffffffffu, lane < 8 && ok);
+        const int id0 = __shfl_sync(0xffffffffu, ids, 0);
+        const uint32_t run = __ballot_sync(0xffffffffu, lane < 8 && ok && ids == id0 + lane);
+        if (run == 0xffu && id0 + 8 <= G.num_pages) {
+          // 8 consecutive pages: one box per (kv, half) block of all of them
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bar_k_full[s], kTileBytes);
+            tma_load_5d(kst + 0 * kKVHalf, &tm_pool, &bar_k_full[s], 0, 0, 0, 0, id0);
+            tma_load_5d(kst + 1 * kKVHalf, &tm_pool, &bar_k_full[s], 0, 0, 0, 1, id0);
+            mbar_arrive_expect_tx(&bar_v_full[s], kTileBytes);
+            tma_load_5d(vst + 0 * kKVHalf, &tm_pool, &bar_v_full[s], 0, 0, 1, 0, id0);
+            tma_load_5d(vst + 1 * kKVHalf, &tm_pool, &bar_v_full[s], 0, 0, 1, 1, id0);
+          }
+          issued = j + 1;
+          __syncwarp();
+          continue;
+        }
         if (lane == 0) {
           if (okm == 0) {
             mbar_arrive(&bar_k_full[s]);
@@ -497,11 +517,35 @@ int encode_rows_map(CUtensorMap* map, const void* base, int B, int C, int H) {
   return AOH_OK;
 }
 
+// The bf16 pool as 5-D (64 elements = 128 B, 16 slots, kv 2, half 2, pages) with
+// (64, 16, 1, 1, 8) boxes: one box is the (kv, half) block of 8 consecutive
+// pages, landing as a [page][slot][128 B] tile (pages are stored pre-swizzled,
+// so the copy itself does not swizzle).
+int encode_pool_runs_map(aoh_kv_cache* c) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(AOH_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[5] = {64, (cuuint64_t)kPage, 2, 2, (cuuint64_t)c->cfg.num_pages};
+  const cuuint64_t strides[4] = {128, (cuuint64_t)kBlockBytes, (cuuint64_t)kHalfBytes,
+                                 (cuuint64_t)kPageBf16Bytes};
+  const cuuint32_t box[5] = {64, (cuuint32_t)kPage, 1, 1, 8};
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(&c->tmap_pool_runs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, c->pool, dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AOH_ERR_CUDA, "cuTensorMapEncodeTiled (pool runs) failed (%d)", (int)r);
+  c->tmap_pool_runs_ok = true;
+  return AOH_OK;
+}
+
 }  // namespace
 
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
                         const void* v_new, void* out, cudaStream_t st) {
   const auto& cf = c->cfg;
+  if (!c->tmap_pool_runs_ok && cf.num_pages > 0) {
+    int rc = encode_pool_runs_map(c);
+    if (rc) return rc;
+  }
   static bool attr_done = false;
   if (!attr_done) {
     int rc = cuda_check(cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -538,7 +582,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.n_qtiles = (q_len + BM - 1) / BM;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
   dim3 grid(a.n_qtiles, a.n_heads);
-  prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, a);
+  prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, c->tmap_pool_runs, a);
   return cuda_check(cudaGetLastError(), "prefill kernel launch");
 }
 
