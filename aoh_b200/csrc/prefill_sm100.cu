@@ -10,32 +10,38 @@
 // the probabilities are rounded to bf16 for P.V, as the reference rounds them
 // to the input dtype.
 //
-// One CTA = 128 query rows (consecutive tokens) of one query head.  Its keys
-// are a sequence of 128-key tiles: first the unit's cached pages (8 pages per
-// tile; each page's four 2 KB (half, K|V) blocks are bulk-copied straight into
-// the 128-byte-swizzled tile layout -- pages are stored pre-swizzled), then the
-// rows of this call's new keys (TMA tensor loads with the same swizzle).
-// Streaming heads list only their sink and ring pages and the chunk rows
-// inside the window, so evicted or out-of-window keys are never loaded.
+// One CTA = the same 128 query rows (consecutive tokens) of two query heads of
+// one KV group (GQA), so both 128x128 query tiles share every K/V tile and
+// every mask; a group with an odd head count leaves one CTA per row block
+// with a single tile.  Keys come as 128-key tiles: first the unit's cached
+// pages (pages are stored pre-swizzled: 8 consecutive page ids are fetched
+// with 4 TMA tensor loads, other tiles with one 2 KB bulk copy per
+// (page, K|V, half)), then the rows of this call's new keys (TMA tensor loads
+// with the 128-byte swizzle).  Streaming heads list only their sink and ring
+// pages and the new rows inside the window.
 //
-// Warp roles (192 threads):
-//   warp 0   producer: Q once, then K and V tiles into two 3-stage rings
-//            (mbarriers); K of a tile is released as soon as its QK^T is
-//            done, so loads run ahead of the PV that still needs V.  A cache
-//            tile whose 8 pages have consecutive ids (the allocator hands out
-//            runs) is fetched with 4 TMA tensor loads over the pool; other
-//            tiles with one 2 KB bulk copy per (page, K|V, half).
-//   warp 1   allocates 512 TMEM columns; lane 0 issues every tcgen05.mma:
-//              S[j%2] = Q K_j^T  (SS: both operands in shared memory, K-major)
-//              O     += P_{j-1} V_{j-1}  (TS: P from TMEM, V MN-major)
-//            and signals completion with tcgen05.commit onto mbarriers.
-//   warps 2-5 softmax: thread r owns query row r = TMEM lane r.  It loads the
-//            row of S, masks it (boundary tiles only), keeps a running max
-//            that is raised only when a tile's max exceeds it by more than
-//            2^8 (then O is rescaled in TMEM), writes P (bf16) to TMEM and
-//            finally writes O / l.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// Warps (352 threads, so each may hold 184 registers):
+//   warp 8      K producer: both Q tiles once, then K tiles into a 3-stage ring.
+//   warp 10     V producer: V tiles into a 2-stage ring (mbarriers); the two
+//               rings are released at different times, so they are fed by
+//               separate warps and neither waits on the other.
+//   warp 9      allocates all 512 TMEM columns; lane 0 issues the MMAs, per
+//               key tile i:  S0 = Q0 K_i^T,  O1 += P1(i-1) V_{i-1},
+//               S1 = Q1 K_i^T,  O0 += P0(i) V_i   (tcgen05, SS for QK^T with
+//               K-major operands, TS for PV with P read from TMEM and V
+//               MN-major).  tcgen05.mma runs in issue order, so P_q (which
+//               overwrites the first 64 columns of S_q in place) is consumed
+//               before the next S_q is written, and O_q is final for tile
+//               i-1 whenever S_q(i) is.
+//   warps 0-3   softmax of tile 0, warps 4-7 of tile 1: thread r owns row r
+//               (TMEM lane r; warp w reaches lanes [32 (w % 4), +32)).  Pass 1 reads S in 32-column chunks for the row
+//               max; pass 2 re-reads them, writes P = 2^(s*scale - m) as bf16
+//               over the consumed columns, and sums the row.  The reference max
+//               is raised only when a tile exceeds it by more than 2^8 (then O
+//               is rescaled in TMEM).  The epilogue writes O / l.
+// TMEM columns: S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512).
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -44,19 +50,20 @@
 namespace aoh {
 namespace {
 
-constexpr int BM = 128;  // query rows per CTA
+constexpr int BM = 128;  // query rows per tile (= CTA row block)
 constexpr int BN = 128;  // keys per tile
-constexpr int kPThreads = 192;
-constexpr int kQBytes = 2 * BM * 128;       // [half][row][128 B]
-constexpr int kKVHalf = BN * 128;           // one 64-dim half of K or V for a tile
-constexpr int kTileBytes = 2 * kKVHalf;     // K (or V) of one tile: [half][key][128 B]
-constexpr int kPStages = 3;                 // separate K and V rings of 3 tiles each
-constexpr int kPSmem = kQBytes + 2 * kPStages * kTileBytes + 1024;
+constexpr int kPThreads = 352;
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
+constexpr int kQTile = 2 * BM * 128;        // one query tile: [half][row][128 B]
+constexpr int kKVHalf = BN * 128;           // one 64-dim half of K or V for a key tile
+constexpr int kTileBytes = 2 * kKVHalf;     // K (or V) of one key tile
+constexpr int kKStages = 3;  // K is released as soon as both QK^T of a tile are issued
+constexpr int kVStages = 2;  // V lives until the second tile's PV, one iteration later
+constexpr int kPSmem = 2 * kQTile + (kKStages + kVStages) * kTileBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
-__device__ __forceinline__ uint32_t col_s(int s) { return s ? 128u : 0u; }    // S0 / S1
-__device__ __forceinline__ uint32_t col_p(int s) { return s ? 448u : 384u; }  // P0 / P1
-constexpr int kMaxHeadsP = 768;
+__device__ __forceinline__ uint32_t col_s(int q) { return q ? 128u : 0u; }    // S_q (P_q in its first 64)
+__device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 256u; }  // O_q
+constexpr int kMaxItemsP = 768;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillArgs {
@@ -64,8 +71,10 @@ struct PrefillArgs {
   CacheGeom geom;
   int layer, T, C, n_qtiles;
   float scale_log2;
-  int n_heads;
-  int head[kMaxHeadsP];  // ((b * Hq + h) << 1) | retrieval, retrieval heads first
+  int n_items;
+  // ((b * Hq + h0) << 2) | ((heads - 1) << 1) | retrieval: heads h0 (and h0+1)
+  // of one KV group; retrieval items first
+  int item[kMaxItemsP];
 };
 
 // The key tiles of one CTA.  Every thread builds the same list.
@@ -160,9 +169,6 @@ struct TileList {
     chunk(j, &r0, &lo, &hi);
     return r0 >= lo && r0 + BN <= hi && r0 + BN - 1 <= i0;
   }
-  __device__ __forceinline__ bool allowed(int p, int qp) const {
-    return p >= 0 && p <= qp && (retr || p < sink || p >= qp - recent);
-  }
 };
 
 __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
@@ -175,52 +181,56 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const __grid_constant__ PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024p(smem_raw);
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kQBytes;                    // K ring: stage s at sK + s * kTileBytes
-  uint8_t* sV = sK + kPStages * kTileBytes;        // V ring
+  uint8_t* sQ = smem;                               // tile q at sQ + q * kQTile
+  uint8_t* sK = smem + 2 * kQTile;                  // K ring: stage s at sK + s * kTileBytes
+  uint8_t* sV = sK + kKStages * kTileBytes;         // V ring
   __shared__ __align__(8) uint64_t bar_q, bar_final;
-  __shared__ __align__(8) uint64_t bar_k_full[kPStages], bar_k_empty[kPStages];
-  __shared__ __align__(8) uint64_t bar_v_full[kPStages], bar_v_empty[kPStages];
-  __shared__ __align__(8) uint64_t bar_s_full[2], bar_s_free[2], bar_p_full[2], bar_o_done[2];
+  __shared__ __align__(8) uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
+  __shared__ __align__(8) uint64_t bar_v_full[kVStages], bar_v_empty[kVStages];
+  __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2];
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
+  // [softmax group][buffer][column]: rows [x, y] of this CTA allowed to see the
+  // key of that column of a masked tile (y < x: none)
+  __shared__ char2 s_kwin[2][2][BN];
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int code = a.head[blockIdx.y];
+  const int code = a.item[blockIdx.y];
   const bool retr = code & 1;
-  const int bh = code >> 1;
-  const int b = bh / G.Hq, h = bh % G.Hq, g = h / G.grp;
-  const int i0 = (a.n_qtiles - 1 - (int)blockIdx.x) * BM;  // heaviest (last) query tiles first
+  const int nq = ((code >> 1) & 1) + 1;  // query tiles in this CTA
+  const int bh = code >> 2;
+  const int b = bh / G.Hq, h0 = bh % G.Hq, g = h0 / G.grp;
+  const int i0 = (a.n_qtiles - 1 - (int)blockIdx.x) * BM;  // heaviest (last) row blocks first
   TileList tl;
   tl.init(retr, a.T, a.C, i0, G);
   const int n_tiles = tl.n_tiles;
 
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tmem_alloc(&s_tmem, kTmemCols);
     tmem_relinquish();
   }
   if (tid == 0) {
     mbar_init(&bar_q, 1);
     mbar_init(&bar_final, 1);
-    for (int s = 0; s < kPStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&bar_k_full[s], 1);
       mbar_init(&bar_k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&bar_v_full[s], 1);
       mbar_init(&bar_v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar_s_full[s], 1);
-      mbar_init(&bar_s_free[s], 128);
-      mbar_init(&bar_p_full[s], 128);
-      mbar_init(&bar_o_done[s], 1);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&bar_s_full[q], 1);
+      mbar_init(&bar_p_full[q], 128);
     }
     s_abort = 0;
     fence_mbar_init();
   }
   // Tile regions never loaded (tail of the last cache tile) must hold finite
   // values: P is 0 there, but 0 * NaN would poison the MMA.
-  for (int i = tid; i < 2 * kPStages * kTileBytes / 16; i += kPThreads)
+  for (int i = tid; i < (kKStages + kVStages) * kTileBytes / 16; i += kPThreads)
     reinterpret_cast<uint4*>(sK)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async_smem();
   tc_fence_before();
@@ -228,14 +238,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp == 0) {
-    // ============================ producer ============================
+  if (warp == kWarpK || warp == kWarpV) {
+    // ============================ producers (K and V) ============================
+    const int kv = warp == kWarpK ? 0 : 1;
+    const int nst = kv ? kVStages : kKStages;
+    uint8_t* ring = kv ? sV : sK;
+    uint64_t* full_b = kv ? bar_v_full : bar_k_full;
+    uint64_t* empty_b = kv ? bar_v_empty : bar_k_empty;
+    const CUtensorMap* rows_map = kv ? &tm_v : &tm_k;
     const int32_t* bt = G.block_table + G.unit_offset[(a.layer * G.B + b) * G.G + g];
     const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bar_q, kQBytes);
-      tma_load_4d(sQ, &tm_q, &bar_q, 0, h, i0, b);
-      tma_load_4d(sQ + kQBytes / 2, &tm_q, &bar_q, 64, h, i0, b);
+    if (kv == 0 && lane == 0) {
+      mbar_arrive_expect_tx(&bar_q, nq * kQTile);
+      for (int q = 0; q < nq; ++q) {
+        tma_load_4d(sQ + q * kQTile, &tm_q, &bar_q, 0, h0 + q, i0, b);
+        tma_load_4d(sQ + q * kQTile + kQTile / 2, &tm_q, &bar_q, 64, h0 + q, i0, b);
+      }
     }
     auto fetch_ids = [&](int j) -> int {
       if (j >= n_tiles || !tl.is_cache(j) || lane >= 8) return -1;
@@ -247,215 +265,233 @@ __global__ void __launch_bounds__(kPThreads, 1)
     for (int j = 0; j < n_tiles; ++j) {
       const int ids = ids_next;
       ids_next = fetch_ids(j + 1);  // page ids of the next tile, in flight during this one
-      const int s = j % kPStages, rnd = j / kPStages;
-      uint8_t* kst = sK + s * kTileBytes;
-      uint8_t* vst = sV + s * kTileBytes;
+      const int s = j % nst, rnd = j / nst;
+      uint8_t* dst = ring + s * kTileBytes;
       if (lane == 0 && rnd > 0 && !s_abort) {
-        if (!mbar_wait(&bar_k_empty[s], (rnd - 1) & 1, G.err)) s_abort = 1;
-        if (!s_abort && !mbar_wait(&bar_v_empty[s], (rnd - 1) & 1, G.err)) s_abort = 1;
+        if (!mbar_wait(&empty_b[s], (rnd - 1) & 1, G.err)) s_abort = 1;
       }
       __syncwarp();
       if (s_abort) break;
       if (tl.is_cache(j)) {
         const bool ok = ids >= 0 && ids < G.num_pages;
         const bool want = lane < 8 && j * 8 + lane < tl.n_pages;
-        if (want && !ok) atomicOr(G.err, kErrBadPage);
+        if (kv == 0 && want && !ok) atomicOr(G.err, kErrBadPage);
         const uint32_t okm = __ballot_sync(0xffffffffu, lane < 8 && ok);
         const int id0 = __shfl_sync(0xffffffffu, ids, 0);
         const uint32_t run = __ballot_sync(0xffffffffu, lane < 8 && ok && ids == id0 + lane);
         if (run == 0xffu && id0 + 8 <= G.num_pages) {
-          // 8 consecutive pages: one box per (kv, half) block of all of them
+          // 8 consecutive pages: one box per half of all of them
           if (lane == 0) {
-            mbar_arrive_expect_tx(&bar_k_full[s], kTileBytes);
-            tma_load_5d(kst + 0 * kKVHalf, &tm_pool, &bar_k_full[s], 0, 0, 0, 0, id0);
-            tma_load_5d(kst + 1 * kKVHalf, &tm_pool, &bar_k_full[s], 0, 0, 0, 1, id0);
-            mbar_arrive_expect_tx(&bar_v_full[s], kTileBytes);
-            tma_load_5d(vst + 0 * kKVHalf, &tm_pool, &bar_v_full[s], 0, 0, 1, 0, id0);
-            tma_load_5d(vst + 1 * kKVHalf, &tm_pool, &bar_v_full[s], 0, 0, 1, 1, id0);
+            mbar_arrive_expect_tx(&full_b[s], kTileBytes);
+            tma_load_5d(dst + 0 * kKVHalf, &tm_pool, &full_b[s], 0, 0, kv, 0, id0);
+            tma_load_5d(dst + 1 * kKVHalf, &tm_pool, &full_b[s], 0, 0, kv, 1, id0);
           }
-          issued = j + 1;
+        } else {
+          if (lane == 0) {
+            if (okm == 0)
+              mbar_arrive(&full_b[s]);
+            else
+              mbar_arrive_expect_tx(&full_b[s], __popc(okm) * (kPageBf16Bytes / 2));
+          }
           __syncwarp();
-          continue;
-        }
-        if (lane == 0) {
-          if (okm == 0) {
-            mbar_arrive(&bar_k_full[s]);
-            mbar_arrive(&bar_v_full[s]);
-          } else {
-            mbar_arrive_expect_tx(&bar_k_full[s], __popc(okm) * (kPageBf16Bytes / 2));
-            mbar_arrive_expect_tx(&bar_v_full[s], __popc(okm) * (kPageBf16Bytes / 2));
+          // lane jp < 8 copies page jp's two 2 KB blocks (halves) of K or V
+          if (lane < 8 && ok) {
+            const uint8_t* src = pool + (size_t)ids * kPageBf16Bytes + kv * kBlockBytes;
+            const int row_off = lane * kPage * 128;
+            bulk_load(dst + 0 * kKVHalf + row_off, src, kBlockBytes, &full_b[s]);
+            bulk_load(dst + 1 * kKVHalf + row_off, src + kHalfBytes, kBlockBytes, &full_b[s]);
           }
-        }
-        __syncwarp();
-        // lane jp < 8 copies page jp's four 2 KB blocks into the K and V tile halves
-        if (lane < 8 && ok) {
-          const uint8_t* src = pool + (size_t)ids * kPageBf16Bytes;
-          const int row_off = lane * kPage * 128;
-          bulk_load(kst + 0 * kKVHalf + row_off, src + 0 * kBlockBytes, kBlockBytes, &bar_k_full[s]);  // K lo
-          bulk_load(kst + 1 * kKVHalf + row_off, src + 2 * kBlockBytes, kBlockBytes, &bar_k_full[s]);  // K hi
-          bulk_load(vst + 0 * kKVHalf + row_off, src + 1 * kBlockBytes, kBlockBytes, &bar_v_full[s]);  // V lo
-          bulk_load(vst + 1 * kKVHalf + row_off, src + 3 * kBlockBytes, kBlockBytes, &bar_v_full[s]);  // V hi
         }
       } else if (lane == 0) {
         int r0, lo, hi;
         tl.chunk(j, &r0, &lo, &hi);
-        mbar_arrive_expect_tx(&bar_k_full[s], kTileBytes);
-        tma_load_4d(kst + 0 * kKVHalf, &tm_k, &bar_k_full[s], 0, g, r0, b);
-        tma_load_4d(kst + 1 * kKVHalf, &tm_k, &bar_k_full[s], 64, g, r0, b);
-        mbar_arrive_expect_tx(&bar_v_full[s], kTileBytes);
-        tma_load_4d(vst + 0 * kKVHalf, &tm_v, &bar_v_full[s], 0, g, r0, b);
-        tma_load_4d(vst + 1 * kKVHalf, &tm_v, &bar_v_full[s], 64, g, r0, b);
+        mbar_arrive_expect_tx(&full_b[s], kTileBytes);
+        tma_load_4d(dst + 0 * kKVHalf, rows_map, &full_b[s], 0, g, r0, b);
+        tma_load_4d(dst + 1 * kKVHalf, rows_map, &full_b[s], 64, g, r0, b);
       }
       issued = j + 1;
       __syncwarp();
     }
     // nothing this CTA issued may still be landing when it exits
     if (lane == 0) {
-      mbar_wait(&bar_q, 0, G.err);
-      for (int j = max(0, issued - kPStages); j < issued; ++j) {
-        mbar_wait(&bar_k_full[j % kPStages], (j / kPStages) & 1, G.err);
-        mbar_wait(&bar_v_full[j % kPStages], (j / kPStages) & 1, G.err);
-      }
+      if (kv == 0) mbar_wait(&bar_q, 0, G.err);
+      for (int j = max(0, issued - nst); j < issued; ++j) mbar_wait(&full_b[j % nst], (j / nst) & 1, G.err);
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ============================ MMA issuer ============================
     if (lane == 0) {
       constexpr uint32_t kIdescQK = idesc_bf16(BM, BN, 0, 0);
       constexpr uint32_t kIdescPV = idesc_bf16(BM, 128, 0, 1);
-      const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(&bar_q, 0, G.err);
       tc_fence_after();
-      auto pv = [&](int t) {
-        const int s = t & 1;
-        if (!mbar_wait(&bar_v_full[t % kPStages], (t / kPStages) & 1, G.err) ||
-            !mbar_wait(&bar_p_full[s], (t >> 1) & 1, G.err)) {
+      auto qk = [&](int q, int i) {
+        const uint32_t q_addr = smem_u32(sQ + q * kQTile);
+        const uint32_t k_addr = smem_u32(sK + (i % kKStages) * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * kKVHalf + (k & 3) * 32;
+          mma_ss(tmem + col_s(q), smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                 kIdescQK, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&bar_s_full[q]);
+      };
+      // O_q += P_q(i) V_i, once the softmax of (q, i) has written P_q(i)
+      auto pv = [&](int q, int i) {
+        if (!mbar_wait(&bar_p_full[q], i & 1, G.err)) {
           s_abort = 1;
           return false;
         }
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + (t % kPStages) * kTileBytes);
+        const uint32_t v_addr = smem_u32(sV + (i % kVStages) * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const uint64_t vdesc = smem_desc_sw128(v_addr + k * 16 * 128, kKVHalf, 1024);
-          mma_ts(tmem + kColO, tmem + col_p(s) + 8 * k, vdesc, kIdescPV, (t > 0 || k > 0) ? 1u : 0u);
-        }
-        mma_commit(&bar_o_done[s]);
-        mma_commit(&bar_v_empty[t % kPStages]);
+        for (int k = 0; k < BN / 16; ++k)
+          mma_ts(tmem + col_o(q), tmem + col_s(q) + 8 * k, smem_desc_sw128(v_addr + k * 16 * 128, kKVHalf, 1024),
+                 kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
         return true;
       };
-      for (int j = 0; j < n_tiles && ok && !s_abort; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&bar_k_full[j % kPStages], (j / kPStages) & 1, G.err)) break;
-        if (j >= 2 && !mbar_wait(&bar_s_free[s], ((j >> 1) - 1) & 1, G.err)) break;
+      for (int i = 0; i < n_tiles && ok && !s_abort; ++i) {
+        const int ks = i % kKStages, vs = i % kVStages;
+        if (!mbar_wait(&bar_k_full[ks], (i / kKStages) & 1, G.err)) break;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + (j % kPStages) * kTileBytes);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * kKVHalf + (k & 3) * 32;
-          const uint64_t adesc = smem_desc_sw128(q_addr + off, 16, 1024);
-          const uint64_t bdesc = smem_desc_sw128(k_addr + off, 16, 1024);
-          mma_ss(tmem + col_s(s), adesc, bdesc, kIdescQK, k > 0 ? 1u : 0u);
+        qk(0, i);
+        if (nq == 2) {
+          if (i > 0) {
+            if (!pv(1, i - 1)) break;
+            mma_commit(&bar_v_empty[(i - 1) % kVStages]);  // V_{i-1} fully consumed
+          }
+          qk(1, i);
         }
-        mma_commit(&bar_s_full[s]);
-        mma_commit(&bar_k_empty[j % kPStages]);
-        if (j >= 1 && !pv(j - 1)) break;
+        mma_commit(&bar_k_empty[ks]);
+        if (!mbar_wait(&bar_v_full[vs], (i / kVStages) & 1, G.err)) break;
+        tc_fence_after();
+        if (!pv(0, i)) break;
+        if (nq == 1) mma_commit(&bar_v_empty[vs]);
       }
-      if (n_tiles > 0 && !s_abort) pv(n_tiles - 1);
-      mma_commit(&bar_final);  // fires once every MMA issued above has completed
+      if (nq == 2 && n_tiles > 0 && !s_abort && pv(1, n_tiles - 1)) mma_commit(&bar_v_empty[(n_tiles - 1) % kVStages]);
+      mma_commit(&bar_final);  // fires once every MMA issued above has completed (both O tiles final)
     }
     __syncwarp();
-  } else {
-    // ============================ softmax (warps 2-5) ============================
+  } else if (warp < 8 && warp / 4 < nq) {
+    // ============================ softmax, tile q ============================
+    const int q = warp / 4;
     const int quarter = warp & 3;
     const int row = 32 * quarter + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+    const uint32_t s_col = lane_base + col_s(q);
     const int qi = i0 + row;
-    const int qp = a.T + qi;
     const float sl2 = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int s = j & 1;
-      if (s_abort || !mbar_wait(&bar_s_full[s], (j >> 1) & 1, G.err)) {
+    int n_masked = 0;  // masked tiles seen so far: picks the key-position buffer
+    // P = 2^(s*scale - m) as bf16, written over the S columns already read
+    // (P for keys [32c, 32c+64) lands in columns [16c, 16c+32)); the masked
+    // and unmasked loops are separate so each is one compact block of code
+    auto exp_pass = [&](auto masked_tag, const char2* kw, float nmu) {
+      constexpr bool kMasked = decltype(masked_tag)::value;
+#pragma unroll
+      for (int c = 0; c < BN / 32; c += 2) {
+        uint32_t sv[64];
+        tmem_ld32(s_col + 32 * c, sv);
+        tmem_ld32(s_col + 32 * c + 32, sv + 32);
+        tc_wait_ld();
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl2, nmu));
+          float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, nmu));
+          if (kMasked) {
+            const char2 w0 = kw[32 * c + 2 * e], w1 = kw[32 * c + 2 * e + 1];
+            if (row < w0.x || row > w0.y) p0 = 0.f;
+            if (row < w1.x || row > w1.y) p1 = 0.f;
+          }
+          l += p0 + p1;
+          pk[e] = pack_bf16(p0, p1);
+        }
+        tmem_st32(s_col + 16 * c, pk);
+      }
+    };
+    for (int i = 0; i < n_tiles; ++i) {
+      if (s_abort || !mbar_wait(&bar_s_full[q], i & 1, G.err)) {
         s_abort = 1;
         break;
       }
       tc_fence_after();
-      uint32_t sv[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + col_s(s) + 32 * c, sv + 32 * c);
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bar_s_free[s]);
-      float mt = -INFINITY;
-      if (tl.full(j)) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const float x = __uint_as_float(sv[c]) * sl2;
-          sv[c] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
+      const bool full = tl.full(i);
+      const char2* kw = s_kwin[q][n_masked & 1];
+      if (!full) {
+        // thread r resolves column r's key once for the group: the rows that
+        // may see it are [p - q0, p + recent - q0] (no upper bound for
+        // retrieval heads and sink positions), q0 the CTA's first query
+        // position.  The two buffers alternate; a thread rewrites one only
+        // after every thread of the group has passed the next masked tile's
+        // barrier, i.e. finished reading it.
+        const int kpos = tl.key_pos(i, row);
+        const int q0 = a.T + i0;
+        int lo = max(kpos - q0, 0);
+        int hi = (retr || kpos < tl.sink) ? BM - 1 : min(kpos + tl.recent - q0, BM - 1);
+        if (kpos < 0 || lo > BM - 1 || hi < lo) {
+          lo = BM - 1;
+          hi = -128;
         }
-      } else {
+        s_kwin[q][n_masked & 1][row] = make_char2((signed char)lo, (signed char)hi);
+        named_bar_sync(1 + q, 128);
+        ++n_masked;
+      }
+      // pass 1: row max of the raw scores (the scale is positive)
+      float mraw = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          float x = __uint_as_float(sv[c]) * sl2;
-          if (!tl.allowed(tl.key_pos(j, c), qp)) x = -INFINITY;
-          sv[c] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
+      for (int c = 0; c < BN / 32; c += 2) {
+        uint32_t sv[64];
+        tmem_ld32(s_col + 32 * c, sv);
+        tmem_ld32(s_col + 32 * c + 32, sv + 32);
+        tc_wait_ld();
+        if (full) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const char2 w = kw[32 * c + e];
+            if (row >= w.x && row <= w.y) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+          }
         }
       }
+      const float mt = mraw * sl2;
       if (m_used == -INFINITY) {
         m_used = mt;  // first tile with an allowed key: O holds zeros so far
       } else if (mt > m_used + kRescaleThreshold) {
-        // raise the reference max: O *= 2^(old - new) once PV_{j-1} has landed
+        // O_q is final for tile i-1 (its PV ran before this S_q(i) in issue order)
         const float alpha = fast_exp2(m_used - mt);
-        if (!mbar_wait(&bar_o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, G.err)) {
-          s_abort = 1;
-          break;
-        }
-        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
-          tmem_ld32(lane_base + kColO + 32 * c, ov);
+          tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
           tc_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st32(lane_base + kColO + 32 * c, ov);
+          tmem_st32(lane_base + col_o(q) + 32 * c, ov);
         }
         tc_wait_st();
         l *= alpha;
         m_used = mt;
       }
-      // P[s] is free once PV_{j-2} has completed
-      if (j >= 2 && !mbar_wait(&bar_o_done[s], ((j - 2) >> 1) & 1, G.err)) {
-        s_abort = 1;
-        break;
-      }
-      const float mu = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t pk[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN / 2; ++c) {
-        const float p0 = fast_exp2(__uint_as_float(sv[2 * c]) - mu);
-        const float p1 = fast_exp2(__uint_as_float(sv[2 * c + 1]) - mu);
-        l += p0 + p1;
-        pk[c] = pack_bf16(p0, p1);
-      }
-      tmem_st32(lane_base + col_p(s), pk);
-      tmem_st32(lane_base + col_p(s) + 32, pk + 32);
+      const float nmu = m_used == -INFINITY ? 0.f : -m_used;
+      if (full)
+        exp_pass(std::false_type{}, kw, nmu);
+      else
+        exp_pass(std::true_type{}, kw, nmu);
       tc_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar_p_full[s]);
+      mbar_arrive(&bar_p_full[q]);
     }
     // epilogue: O / l -> bf16 row of the output
-    const int last = n_tiles - 1;
-    if (!s_abort && n_tiles > 0 && mbar_wait(&bar_o_done[last & 1], (last >> 1) & 1, G.err)) {
+    if (!s_abort && n_tiles > 0 && mbar_wait(&bar_final, 0, G.err)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h) * kHeadDim;
+      __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h0 + q) * kHeadDim;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t ov[32];
-        tmem_ld32(lane_base + kColO + 32 * c, ov);
+        tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
         tc_wait_ld();
         uint32_t pk[16];
 #pragma unroll
@@ -473,7 +509,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   // ============================ teardown ============================
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     if (lane == 0) mbar_wait(&bar_final, 0, G.err);  // every MMA has completed
     __syncwarp();
     tc_fence_after();
@@ -481,9 +517,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// host side
-// ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -539,6 +572,7 @@ int encode_pool_runs_map(aoh_kv_cache* c) {
 
 }  // namespace
 
+
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
                         const void* v_new, void* out, cudaStream_t st) {
   const auto& cf = c->cfg;
@@ -555,20 +589,23 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     attr_done = true;
   }
   PrefillArgs a;
-  a.n_heads = 0;
+  a.n_items = 0;
   const int grp = cf.num_q_heads / cf.num_kv_heads;
-  for (int pass = 0; pass < 2; ++pass)  // retrieval heads (heavy) first
+  for (int pass = 0; pass < 2; ++pass)  // retrieval items (heavy) first
     for (int b = 0; b < cf.batch; ++b)
-      for (int h = 0; h < cf.num_q_heads; ++h) {
-        const int g = h / grp;
+      for (int g = 0; g < cf.num_kv_heads; ++g) {
         if (!c->owned[c->unit(layer, b, g)]) continue;
         const bool r = c->retrieval(layer, g);
         if (r != (pass == 0)) continue;
-        if (a.n_heads >= kMaxHeadsP)
-          return fail(AOH_ERR_UNSUPPORTED, "prefill: more than %d (sequence, query head) pairs", kMaxHeadsP);
-        a.head[a.n_heads++] = ((b * cf.num_q_heads + h) << 1) | (r ? 1 : 0);
+        for (int j = 0; j < grp; j += 2) {  // pairs of query heads of the group
+          if (a.n_items >= kMaxItemsP)
+            return fail(AOH_ERR_UNSUPPORTED, "prefill: more than %d (sequence, head pair) items", kMaxItemsP);
+          const int h0 = g * grp + j;
+          const int heads = grp - j >= 2 ? 2 : 1;
+          a.item[a.n_items++] = ((b * cf.num_q_heads + h0) << 2) | ((heads - 1) << 1) | (r ? 1 : 0);
+        }
       }
-  if (a.n_heads == 0 || q_len == 0) return AOH_OK;
+  if (a.n_items == 0 || q_len == 0) return AOH_OK;
   CUtensorMap tq, tk, tv;
   int rc = encode_rows_map(&tq, q, cf.batch, q_len, cf.num_q_heads);
   if (!rc) rc = encode_rows_map(&tk, k_new, cf.batch, q_len, cf.num_kv_heads);
@@ -581,7 +618,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.C = q_len;
   a.n_qtiles = (q_len + BM - 1) / BM;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
-  dim3 grid(a.n_qtiles, a.n_heads);
+  dim3 grid(a.n_qtiles, a.n_items);
   prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, c->tmap_pool_runs, a);
   return cuda_check(cudaGetLastError(), "prefill kernel launch");
 }
