@@ -20,9 +20,10 @@
 // with the 128-byte swizzle).  Streaming heads list only their sink and ring
 // pages and the new rows inside the window.
 //
-// Warps (352 threads, so each may hold 184 registers):
-//   warp 8      K producer: both Q tiles once, then K tiles into a 3-stage ring.
-//   warp 10     V producer: V tiles into a 2-stage ring (mbarriers); the two
+// Warps (384 threads; registers are moved from warpgroup 2 to the softmax
+// warpgroups with setmaxnreg):
+//   warp 8      K producer: both Q tiles once, then K tiles into a 2-stage ring.
+//   warp 10     V producer: V tiles into a 3-stage ring (mbarriers); the two
 //               rings are released at different times, so they are fed by
 //               separate warps and neither waits on the other.
 //   warp 9      allocates all 512 TMEM columns; lane 0 issues the MMAs, per
@@ -52,13 +53,22 @@ namespace {
 
 constexpr int BM = 128;  // query rows per tile (= CTA row block)
 constexpr int BN = 128;  // keys per tile
-constexpr int kPThreads = 352;
-constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
+constexpr int kPThreads = 384;
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // warp 11 only completes warpgroup 2
+// Registers per thread: the kernel is launched with kRegsLaunch (the most 384
+// threads may hold); warpgroup 2 (loads, MMA issue) then gives registers
+// back and the two softmax warpgroups take them.  The shares must fit the
+// launch total: 2 * 128 * kRegsSoftmax + 128 * kRegsOther <= 384 * kRegsLaunch.
+constexpr int kRegsLaunch = 168, kRegsSoftmax = 208, kRegsOther = 88;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kPThreads * kRegsLaunch, "register split");
 constexpr int kQTile = 2 * BM * 128;        // one query tile: [half][row][128 B]
 constexpr int kKVHalf = BN * 128;           // one 64-dim half of K or V for a key tile
 constexpr int kTileBytes = 2 * kKVHalf;     // K (or V) of one key tile
-constexpr int kKStages = 3;  // K is released as soon as both QK^T of a tile are issued
-constexpr int kVStages = 2;  // V lives until the second tile's PV, one iteration later
+// A K stage is freed once both QK^T of its tile complete, a V stage only after
+// the second tile's PV one iteration later: V gets the deeper ring so that
+// each load has about two iterations to land.
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
 constexpr int kPSmem = 2 * kQTile + (kKStages + kVStages) * kTileBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int q) { return q ? 128u : 0u; }    // S_q (P_q in its first 64)
@@ -171,6 +181,21 @@ struct TileList {
   }
 };
 
+// 2^x on the FMA pipe, for x <= 8: x = j + f with j = round(x) (adding
+// 1.5 * 2^23 rounds to an integer held in the low mantissa bits) and f in
+// [-0.5, 0.5]; 2^f is a cubic fitted for least maximum relative error on that
+// interval (7.5e-5, below half a bf16 ulp of P), and j is added to its exponent
+// field.  x is clamped to -126 so the exponent stays in range.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  float p = fmaf(f, 0.05517132f, 0.24261054f);
+  p = fmaf(p, f, 0.69326097f);
+  p = fmaf(p, f, 0.99992812f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
@@ -238,6 +263,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  // Each warpgroup sets its register budget first, so the code of its roles
+  // is compiled (and runs) under that budget.
+  if (warp >= 8) {
+  setmaxnreg_dec<kRegsOther>();
   if (warp == kWarpK || warp == kWarpV) {
     // ============================ producers (K and V) ============================
     const int kv = warp == kWarpK ? 0 : 1;
@@ -371,7 +400,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mma_commit(&bar_final);  // fires once every MMA issued above has completed (both O tiles final)
     }
     __syncwarp();
-  } else if (warp < 8 && warp / 4 < nq) {
+  }
+  } else {
+  setmaxnreg_inc<kRegsSoftmax>();
+  if (warp / 4 < nq) {
     // ============================ softmax, tile q ============================
     const int q = warp / 4;
     const int quarter = warp & 3;
@@ -382,22 +414,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const float sl2 = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     int n_masked = 0;  // masked tiles seen so far: picks the key-position buffer
-    // P = 2^(s*scale - m) as bf16, written over the S columns already read
-    // (P for keys [32c, 32c+64) lands in columns [16c, 16c+32)); the masked
-    // and unmasked loops are separate so each is one compact block of code
-    auto exp_pass = [&](auto masked_tag, const char2* kw, float nmu) {
+    // P = 2^(s*scale - m) as bf16 over the first 64 columns of S (the whole
+    // row is in registers by then).  One pair in four is computed by the
+    // polynomial on the FMA pipe instead of the MUFU.  The masked and
+    // unmasked loops are separate so each is one compact block of code.
+    auto exp_pass = [&](auto masked_tag, const uint32_t* sv, const char2* kw, float nmu) {
       constexpr bool kMasked = decltype(masked_tag)::value;
 #pragma unroll
       for (int c = 0; c < BN / 32; c += 2) {
-        uint32_t sv[64];
-        tmem_ld32(s_col + 32 * c, sv);
-        tmem_ld32(s_col + 32 * c + 32, sv + 32);
-        tc_wait_ld();
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl2, nmu));
-          float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, nmu));
+          const float x0 = fmaf(__uint_as_float(sv[32 * c + 2 * e]), sl2, nmu);
+          const float x1 = fmaf(__uint_as_float(sv[32 * c + 2 * e + 1]), sl2, nmu);
+          float p0, p1;
+          if ((e & 3) == 3) {
+            p0 = exp2_poly(x0);
+            p1 = exp2_poly(x1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
           if (kMasked) {
             const char2 w0 = kw[32 * c + 2 * e], w1 = kw[32 * c + 2 * e + 1];
             if (row < w0.x || row > w0.y) p0 = 0.f;
@@ -436,23 +473,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
         named_bar_sync(1 + q, 128);
         ++n_masked;
       }
-      // pass 1: row max of the raw scores (the scale is positive)
+      uint32_t sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_col + 32 * c, sv + 32 * c);
+      tc_wait_ld();
+      // row max of the raw scores (the scale is positive)
       float mraw = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < BN / 32; c += 2) {
-        uint32_t sv[64];
-        tmem_ld32(s_col + 32 * c, sv);
-        tmem_ld32(s_col + 32 * c + 32, sv + 32);
-        tc_wait_ld();
-        if (full) {
+        for (int e = 0; e < BN; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+      } else {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const char2 w = kw[32 * c + e];
-            if (row >= w.x && row <= w.y) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
-          }
+        for (int e = 0; e < BN; ++e) {
+          const char2 w = kw[e];
+          if (row >= w.x && row <= w.y) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
         }
       }
       const float mt = mraw * sl2;
@@ -476,9 +510,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       const float nmu = m_used == -INFINITY ? 0.f : -m_used;
       if (full)
-        exp_pass(std::false_type{}, kw, nmu);
+        exp_pass(std::false_type{}, sv, kw, nmu);
       else
-        exp_pass(std::true_type{}, kw, nmu);
+        exp_pass(std::true_type{}, sv, kw, nmu);
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full[q]);
@@ -504,6 +538,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
       }
     }
+  }
+
   }
 
   // ============================ teardown ============================
@@ -586,6 +622,14 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
                                              kPSmem),
                         "prefill: smem attribute");
     if (rc) return rc;
+    // the warpgroups' register shares are carved out of the launch allocation:
+    // a kernel built with fewer registers per thread could not satisfy them
+    cudaFuncAttributes fa;
+    rc = cuda_check(cudaFuncGetAttributes(&fa, prefill_bf16_kernel), "prefill: kernel attributes");
+    if (rc) return rc;
+    if (fa.numRegs < kRegsLaunch)
+      return fail(AOH_ERR_CUDA, "prefill kernel built with %d registers per thread, %d needed by its register split",
+                  fa.numRegs, kRegsLaunch);
     attr_done = true;
   }
   PrefillArgs a;
