@@ -96,6 +96,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// mbar_wait for a converged warp: every lane polls, and lane 0's outcome is
+// returned to all, so the warp stays converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 // ----------------------------------------------------------------------------
 // TMA
 // ----------------------------------------------------------------------------
@@ -137,12 +144,18 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// The tcgen05 issue helpers below are executed by a whole converged warp with
+// identical operands (so the compiler can keep them in uniform registers);
+// lane 0 alone issues the instruction.  Commits and the MMAs they track are
+// thus issued by the same thread.
+//
 // D[tmem] (+)= A[smem desc] * B[smem desc]  (kind::f16, one CTA)
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, l;\n\t.reg .u32 lid;\n\tmov.u32 lid, %%laneid;\n\tsetp.eq.u32 l, lid, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -150,15 +163,18 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, l;\n\t.reg .u32 lid;\n\tmov.u32 lid, %%laneid;\n\tsetp.eq.u32 l, lid, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread completes.
+// Arrive (once) on `bar` when every tcgen05.mma issued so far by lane 0 completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred l;\n\t.reg .u32 lid;\n\tmov.u32 lid, %%laneid;\n\tsetp.eq.u32 l, lid, 0;\n\t"
+      "@l tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
 // 32 lanes x 32 columns of 32-bit from TMEM (this warp's lane quarter)

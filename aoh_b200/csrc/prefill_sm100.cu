@@ -181,19 +181,58 @@ struct TileList {
   }
 };
 
-// 2^x on the FMA pipe, for x <= 8: x = j + f with j = round(x) (adding
-// 1.5 * 2^23 rounds to an integer held in the low mantissa bits) and f in
-// [-0.5, 0.5]; 2^f is a cubic fitted for least maximum relative error on that
-// interval (7.5e-5, below half a bf16 ulp of P), and j is added to its exponent
-// field.  x is clamped to -126 so the exponent stays in range.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = __fadd_rn(x, 12582912.f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
-  float p = fmaf(f, 0.05517132f, 0.24261054f);
-  p = fmaf(p, f, 0.69326097f);
-  p = fmaf(p, f, 0.99992812f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Two fp32 lanes in one 64-bit register, for the packed f32x2 arithmetic of
+// sm_100 (one instruction per pair on the FMA pipe).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair, on the FMA pipe, for -inf < x <= 8: x = j + f with
+// j = round(x) (adding 1.5 * 2^23 rounds to an integer held in the low mantissa
+// bits) and f in [-0.5, 0.5]; 2^f is a cubic fitted for least maximum relative
+// error on that interval (7.5e-5, below half a bf16 ulp of P), and j is added
+// to its exponent field.  x is clamped to -126 so the exponent stays in range
+// (2^-126 then stands for anything smaller).
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t magic = f2_pack(12582912.f, 12582912.f);
+  const uint64_t t = f2_add(x, magic);
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  uint64_t p = f2_fma(f, f2_pack(0.05517132f, 0.05517132f), f2_pack(0.24261054f, 0.24261054f));
+  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, f, f2_pack(0.99992812f, 0.99992812f));
+  float q0, q1, t0, t1;
+  f2_unpack(p, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
@@ -348,10 +387,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else if (warp == kWarpMma) {
     // ============================ MMA issuer ============================
-    if (lane == 0) {
+    // The whole warp runs this loop; lane 0 issues inside the helpers.
+    {
       constexpr uint32_t kIdescQK = idesc_bf16(BM, BN, 0, 0);
       constexpr uint32_t kIdescPV = idesc_bf16(BM, 128, 0, 1);
-      bool ok = mbar_wait(&bar_q, 0, G.err);
+      bool ok = mbar_wait_warp(&bar_q, 0, G.err);
       tc_fence_after();
       auto qk = [&](int q, int i) {
         const uint32_t q_addr = smem_u32(sQ + q * kQTile);
@@ -366,7 +406,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       };
       // O_q += P_q(i) V_i, once the softmax of (q, i) has written P_q(i)
       auto pv = [&](int q, int i) {
-        if (!mbar_wait(&bar_p_full[q], i & 1, G.err)) {
+        if (!mbar_wait_warp(&bar_p_full[q], i & 1, G.err)) {
           s_abort = 1;
           return false;
         }
@@ -380,7 +420,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       };
       for (int i = 0; i < n_tiles && ok && !s_abort; ++i) {
         const int ks = i % kKStages, vs = i % kVStages;
-        if (!mbar_wait(&bar_k_full[ks], (i / kKStages) & 1, G.err)) break;
+        if (!mbar_wait_warp(&bar_k_full[ks], (i / kKStages) & 1, G.err)) break;
         tc_fence_after();
         qk(0, i);
         if (nq == 2) {
@@ -391,11 +431,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
           qk(1, i);
         }
         mma_commit(&bar_k_empty[ks]);
-        if (!mbar_wait(&bar_v_full[vs], (i / kVStages) & 1, G.err)) break;
+        if (!mbar_wait_warp(&bar_v_full[vs], (i / kVStages) & 1, G.err)) break;
         tc_fence_after();
         if (!pv(0, i)) break;
         if (nq == 1) mma_commit(&bar_v_empty[vs]);
       }
+      __syncwarp();
       if (nq == 2 && n_tiles > 0 && !s_abort && pv(1, n_tiles - 1)) mma_commit(&bar_v_empty[(n_tiles - 1) % kVStages]);
       mma_commit(&bar_final);  // fires once every MMA issued above has completed (both O tiles final)
     }
@@ -412,35 +453,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t s_col = lane_base + col_s(q);
     const int qi = i0 + row;
     const float sl2 = a.scale_log2;
-    float m_used = -INFINITY, l = 0.f;
+    float m_used = -INFINITY;
     int n_masked = 0;  // masked tiles seen so far: picks the key-position buffer
     // P = 2^(s*scale - m) as bf16 over the first 64 columns of S (the whole
-    // row is in registers by then).  One pair in four is computed by the
-    // polynomial on the FMA pipe instead of the MUFU.  The masked and
-    // unmasked loops are separate so each is one compact block of code.
-    auto exp_pass = [&](auto masked_tag, const uint32_t* sv, const char2* kw, float nmu) {
-      constexpr bool kMasked = decltype(masked_tag)::value;
+    // row is in registers by then); the row sum goes to 8 partial sums.  On
+    // unmasked tiles three pairs in eight are computed by the polynomial on
+    // the FMA pipe instead of the MUFU; masked tiles (their masked scores set
+    // to -inf) use the MUFU alone, whose 2^-inf is exactly 0.
+    uint64_t l2[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) l2[k] = f2_pack(0.f, 0.f);
+    auto exp_pass = [&](auto poly_tag, const uint32_t* sv, float nmu) {
+      constexpr bool kPoly = decltype(poly_tag)::value;
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmu2 = f2_pack(nmu, nmu);
 #pragma unroll
       for (int c = 0; c < BN / 32; c += 2) {
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float x0 = fmaf(__uint_as_float(sv[32 * c + 2 * e]), sl2, nmu);
-          const float x1 = fmaf(__uint_as_float(sv[32 * c + 2 * e + 1]), sl2, nmu);
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[32 * c + 2 * e]), __uint_as_float(sv[32 * c + 2 * e + 1])),
+                                     sl2x2, nmu2);
           float p0, p1;
-          if ((e & 3) == 3) {
-            p0 = exp2_poly(x0);
-            p1 = exp2_poly(x1);
+          if (kPoly && (e & 7) >= 5) {
+            exp2_poly2(x2, p0, p1);
           } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
             p0 = fast_exp2(x0);
             p1 = fast_exp2(x1);
           }
-          if (kMasked) {
-            const char2 w0 = kw[32 * c + 2 * e], w1 = kw[32 * c + 2 * e + 1];
-            if (row < w0.x || row > w0.y) p0 = 0.f;
-            if (row < w1.x || row > w1.y) p1 = 0.f;
-          }
-          l += p0 + p1;
+          l2[e & 3] = f2_add(l2[e & 3], f2_pack(p0, p1));
           pk[e] = pack_bf16(p0, p1);
         }
         tmem_st32(s_col + 16 * c, pk);
@@ -477,18 +519,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_col + 32 * c, sv + 32 * c);
       tc_wait_ld();
-      // row max of the raw scores (the scale is positive)
-      float mraw = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int e = 0; e < BN; ++e) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
-      } else {
+      if (!full) {
 #pragma unroll
         for (int e = 0; e < BN; ++e) {
           const char2 w = kw[e];
-          if (row >= w.x && row <= w.y) mraw = fmaxf(mraw, __uint_as_float(sv[e]));
+          if (row < w.x || row > w.y) sv[e] = __float_as_uint(-INFINITY);
         }
       }
+      // row max of the raw scores (the scale is positive): 8 independent
+      // three-input max chains, then their maximum
+      float mx[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(__uint_as_float(sv[2 * k]), __uint_as_float(sv[2 * k + 1]));
+#pragma unroll
+      for (int e = 16; e < BN; e += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mx[k] = fmax3(mx[k], __uint_as_float(sv[e + 2 * k]), __uint_as_float(sv[e + 2 * k + 1]));
+      const float mraw = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const float mt = mraw * sl2;
       if (m_used == -INFINITY) {
         m_used = mt;  // first tile with an allowed key: O holds zeros so far
@@ -505,14 +553,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
           tmem_st32(lane_base + col_o(q) + 32 * c, ov);
         }
         tc_wait_st();
-        l *= alpha;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) l2[k] = f2_fma(l2[k], f2_pack(alpha, alpha), f2_pack(0.f, 0.f));
         m_used = mt;
       }
       const float nmu = m_used == -INFINITY ? 0.f : -m_used;
       if (full)
-        exp_pass(std::false_type{}, sv, kw, nmu);
+        exp_pass(std::true_type{}, sv, nmu);
       else
-        exp_pass(std::true_type{}, sv, kw, nmu);
+        exp_pass(std::false_type{}, sv, nmu);
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full[q]);
@@ -520,6 +569,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // epilogue: O / l -> bf16 row of the output
     if (!s_abort && n_tiles > 0 && mbar_wait(&bar_final, 0, G.err)) {
       tc_fence_after();
+      float l = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float u, v;
+        f2_unpack(l2[k], u, v);
+        l += u + v;
+      }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h0 + q) * kHeadDim;
 #pragma unroll
