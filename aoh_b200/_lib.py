@@ -68,7 +68,14 @@ _SIGNATURES = {
                                          C.c_size_t, _vp]),
     "aoh_partition": (C.c_int, [C.POINTER(C.c_uint8), _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                 C.POINTER(_i32)]),
+    "aoh_shared_alloc": (C.c_int, [C.c_size_t, C.POINTER(_vp), _vp]),
+    "aoh_shared_free": (C.c_int, [_vp]),
+    "aoh_shared_open": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "aoh_shared_close": (C.c_int, [_vp]),
+    "aoh_kv_set_peers": (C.c_int, [_vp, _i32, _i32, C.POINTER(_vp), C.c_size_t, C.POINTER(_vp)]),
+    "aoh_gather_wait": (C.c_int, [_vp, _i32, _i32, _vp]),
 }
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 _lock = threading.Lock()

@@ -116,7 +116,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 }
 
 // Non-tensor bulk copy global -> shared (16-byte aligned, size multiple of 16),
-// completion signalled on an mbarrier.  No multicast.
+// completion signalled on an mbarrier; this CTA's shared memory is the only destination.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -77,7 +77,34 @@ struct DecodeArgs {
   float scale_log2;  // D^-0.5 * log2(e)
   float* ws;         // per-cluster partials, (kMaxCtas / kCluster) x kPartialFloats
   int* counters;     // kMaxUnits tickets, zero between launches
+  // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
+  // bytes for every rank r (its output region as mapped here), then the flag
+  // (layer, unit) of every rank's flag array is set to T + 1
+  int n_ranks;
+  long long out_delta[kMaxRanks];
+  int32_t* flags[kMaxRanks];
 };
+
+// Store one output element (and, when gathering, the same element in every
+// rank's output region).
+__device__ __forceinline__ void store_out(const DecodeArgs& a, __nv_bfloat16* p, float v) {
+  const __nv_bfloat16 h = __float2bfloat16(v);
+  if (a.n_ranks == 0) {
+    *p = h;
+    return;
+  }
+  for (int r = 0; r < a.n_ranks; ++r) *reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(p) + a.out_delta[r]) = h;
+}
+
+// The unit's rows are stored everywhere and the caller's barrier ordered every
+// writer before this thread: the release stores (system scope, cumulative over
+// what the barrier ordered before them) publish (layer, unit) = T + 1 to every
+// rank.
+__device__ __forceinline__ void publish_unit(const DecodeArgs& a, int bg, int T) {
+  const int idx = a.layer * a.geom.B * a.geom.G + bg;
+  for (int r = 0; r < a.n_ranks; ++r)
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(a.flags[r] + idx), "r"(T + 1) : "memory");
+}
 
 // A unit's compact page list: retrieval pages 0..ceil(T/16)-1; streaming the
 // written sink pages then the written ring pages.
@@ -449,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       L += s_l[w][qq] * f;
     }
     if (nsplit == 1) {
-      out_u[e] = __float2bfloat16(acc / L);
+      store_out(a, out_u + e, acc / L);
     } else {
       cp_o[qq][d] = acc;
       if (d == 0) {
@@ -457,6 +484,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         cp_l[qq] = L;
       }
     }
+  }
+
+  if (nsplit == 1 && a.n_ranks > 0) {
+    __syncthreads();  // every row of the unit is stored
+    if (tid == 0) publish_unit(a, bg, T);
   }
 
   if (nsplit > 1) {
@@ -548,10 +580,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16; ++j) acc[j & 3] += v[j] * sw[(k + j) * kMaxGrp + qq];
       }
       for (; k < nk; ++k) acc[0] += __ldcg(po + (size_t)k * kPartialFloats) * sw[k * kMaxGrp + qq];
-      out_u[e] = __float2bfloat16((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      store_out(a, out_u + e, (acc[0] + acc[1]) + (acc[2] + acc[3]));
+    }
+    // the ticket is reset before the unit is published: once every unit of the
+    // layer is published, the next kernel may reuse the workspace
+    if (rank == 0 && tid == 0) a.counters[u] = 0;
+    if (a.n_ranks > 0) {
+      cluster_sync_all();  // every CTA of the cluster stored its slice of the unit
+      if (rank == 0 && tid == 0) publish_unit(a, bg, T);
     }
     if (rank != 0) return;
-    if (tid == 0) a.counters[u] = 0;  // ready for the next launch
   }
 
   // ===================== append the new token (after every read of the unit) =====================
@@ -705,6 +743,24 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
   a.counters = static_cast<int*>(ws);
   a.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
+  a.n_ranks = 0;
+  for (int r = 0; r < kMaxRanks; ++r) {
+    a.out_delta[r] = 0;
+    a.flags[r] = nullptr;
+  }
+  if (c->n_ranks > 0) {
+    // the layer's whole output (B, 1, Hq, D) must lie in this rank's region
+    const char* own = c->out_regions[c->rank];
+    const char* o = static_cast<const char*>(out);
+    const size_t span = (size_t)cf.batch * cf.num_q_heads * kHeadDim * sizeof(__nv_bfloat16);
+    if (o < own || (size_t)(o - own) + span > c->out_bytes)
+      return fail(AOH_ERR_INVALID_ARGUMENT, "decode: with peers attached, out must lie in this rank's output region");
+    a.n_ranks = c->n_ranks;
+    for (int r = 0; r < c->n_ranks; ++r) {
+      a.out_delta[r] = (long long)(c->out_regions[r] - own);
+      a.flags[r] = c->flag_arrays[r];
+    }
+  }
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(grid, st, attr, true);
   return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");

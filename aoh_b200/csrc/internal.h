@@ -16,6 +16,7 @@ namespace aoh {
 
 constexpr int kHeadDim = 128;
 constexpr int kPage = 16;
+constexpr int kMaxRanks = 8;  // GPUs of one node taking part in an output gather
 
 // Sets the thread's last-error message and returns `code`.
 int fail(int code, const char* fmt, ...);
@@ -62,6 +63,11 @@ struct aoh_kv_cache {
   // consecutive pages gathers one (kv, half) block of each into a 128-key tile
   CUtensorMap tmap_pool_runs;
   bool tmap_pool_runs_ok = false;
+  // output gather across the ranks of a node (aoh_kv_set_peers); n_ranks = 0: off
+  int n_ranks = 0, rank = 0;
+  char* out_regions[aoh::kMaxRanks] = {};
+  size_t out_bytes = 0;
+  int32_t* flag_arrays[aoh::kMaxRanks] = {};
 
   int unit(int layer, int b, int g) const { return (layer * cfg.batch + b) * cfg.num_kv_heads + g; }
   bool retrieval(int layer, int g) const { return labels[layer * cfg.num_kv_heads + g] != 0; }
@@ -77,6 +83,8 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
                        const void* v_new, void* out, void* ws, size_t ws_bytes, cudaStream_t st,
                        const int* past_len_dev);
 int launch_set_length(aoh_kv_cache* c, int value, int add, cudaStream_t st);
+// Gather-wait kernel for `layer` at position past_len (device length if past_len_dev).
+int launch_gather_wait(aoh_kv_cache* c, int layer, int past_len, const int* past_len_dev, cudaStream_t st);
 size_t decode_workspace_bytes(const aoh_kv_cache* c);
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
                         const void* v_new, void* out, cudaStream_t st);

@@ -12,6 +12,10 @@ layer's kernel finishes.
 
 Inputs and outputs are the fixed tensors given at construction; write a
 step's q/k/v into them before ``replay()`` (or let producing kernels do so).
+
+With a ``PeerGather`` (multi-GPU, one process per GPU) each layer's decode
+kernel also stores its units' outputs into every rank's output region, and
+the graph waits for all ranks' units after each layer (the layer boundary).
 """
 from __future__ import annotations
 
@@ -33,7 +37,7 @@ class DecodeStepGraph:
     """
 
     def __init__(self, cache: AoHKVCache, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                 out: torch.Tensor, max_steps: int, layers=None):
+                 out: torch.Tensor, max_steps: int, layers=None, gather=None):
         if cache.dtype != torch.bfloat16:
             raise ValueError("graph decode needs a bfloat16 cache")
         self.cache = cache
@@ -44,15 +48,22 @@ class DecodeStepGraph:
             if not t.is_contiguous() or t.dtype != torch.bfloat16 or t.device != cache.device:
                 raise ValueError(f"{name} must be a contiguous bf16 tensor on {cache.device}")
         self.q, self.k, self.v, self.out = q, k, v, out
+        self.gather = gather
         cache.reserve(cache.kv_seq_len + max_steps + 1)
         self._L = cache._L
         self._ws = cache.decode_workspace()
         self._set_length(cache.kv_seq_len)
         # the first launch configures kernel attributes (not capturable): run the
         # step once eagerly with the length not advanced -- it appends at the
-        # current position, which the first replay rewrites with the same data
-        self._launch_layers()
+        # current position, which the first replay rewrites with the same data.
+        # A gather is detached meanwhile: the eager step must publish no flags
+        # the first replay (same position) would then find already set.
+        if gather is not None:
+            gather.detach()
+        self._launch_layers(with_gather=False)
         torch.cuda.synchronize(cache.device)
+        if gather is not None:
+            gather.attach()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._launch_layers()
@@ -65,7 +76,7 @@ class DecodeStepGraph:
         _lib.check(self._L.aoh_kv_set_length(self.cache._h, n, C.c_void_p(_lib.stream_handle())),
                    "aoh_kv_set_length")
 
-    def _launch_layers(self) -> None:
+    def _launch_layers(self, with_gather: bool = True) -> None:
         st = C.c_void_p(_lib.stream_handle())
         h = self.cache._h
         for i, layer in enumerate(self.layers):
@@ -74,6 +85,8 @@ class DecodeStepGraph:
                                          C.c_void_p(self.out[i].data_ptr()), C.c_void_p(self._ws.data_ptr()),
                                          self._ws.numel(), st)
             _lib.check(rc, "aoh_attn_decode")
+            if with_gather and self.gather is not None:
+                _lib.check(self._L.aoh_gather_wait(h, layer, _lib.PAST_LEN_DEVICE, st), "aoh_gather_wait")
 
     def replay(self) -> None:
         """Run one decode step (all captured layers) and advance the length."""

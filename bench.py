@@ -11,9 +11,13 @@ Workload (one step = one decode token through every layer's attention):
   --gpus N > 1 (one process per GPU, torchrun): N sequences of 128K, the
   (sequence, KV head) units of every layer partitioned across ranks by the
   longest-processing-time rule on touched KV tokens; each rank attends its
-  units, then the outputs are all-gathered over NCCL at the layer boundary
-  (weak scaling: per-GPU work is fixed).  ``value`` is microseconds per
-  (layer, sequence) for the whole job.
+  units and its decode kernel stores every finished unit's output into all
+  ranks' output buffers over NVLink (CUDA IPC peer pointers) with a flag per
+  unit; a wait kernel per layer is the layer boundary, and the whole step is
+  one CUDA graph (weak scaling: per-GPU work is fixed).  ``--gather nccl``
+  instead all-gathers the outputs with NCCL after each layer, eagerly (the
+  library-collective baseline).  ``value`` is microseconds per (layer,
+  sequence) for the whole job.
 
 Also reported on the same line: the decode kernel's HBM roofline fraction,
 an end-to-end number through the public API with host buffers, the CPU
@@ -215,7 +219,7 @@ def run_aoh(args):
                                             T_CTX, SINK, RECENT, world,
                                             owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
     owned = (owner == rank).astype(np.uint8)
-    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 4096
+    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 4096 + 5 * 400
     cache = AoHKVCache(labels, HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
                        dtype=torch.bfloat16, device=dev, owned=owned, reserve_all=True)
     gen = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
@@ -227,10 +231,17 @@ def run_aoh(args):
     q = torch.randn((L_LAYERS, B, 1, HQ, D), generator=gen, device=dev).to(torch.bfloat16)
     kn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
     vn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
-    out = torch.zeros((L_LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
+    peer = None
+    if world > 1 and args.gather == "peer":
+        from aoh_b200.gather import PeerGather
+        peer = PeerGather(cache, out_shape=(L_LAYERS, B, 1, HQ, D))
+        out = peer.out  # decoded straight into the shared output region
+        out.zero_()
+    else:
+        out = torch.zeros((L_LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
 
-    # gather plumbing (world > 1): pack owned (b, g) head groups, all-gather, unpack
-    if world > 1:
+    # NCCL gather plumbing (--gather nccl): pack owned (b, g) head groups, all-gather, unpack
+    if world > 1 and peer is None:
         grp = HQ // G
         packs, unpack = [], []
         max_units = max(int((owner[l] == r).sum()) for l in range(L_LAYERS) for r in range(world))
@@ -257,9 +268,12 @@ def run_aoh(args):
             flat.index_copy_(0, dst, gathered.index_select(0, src))
 
     graph = None
-    if world == 1:
+    if world == 1 or peer is not None:
         from aoh_b200.graph import DecodeStepGraph
-        graph = DecodeStepGraph(cache, q, kn, vn, out, max_steps=args.warmup + args.steps + args.e2e_steps + 8)
+        graph = DecodeStepGraph(cache, q, kn, vn, out,
+                                max_steps=args.warmup + args.steps + args.e2e_steps + 8 + 5 * 400,
+                                gather=peer)
+    used_graph = graph is not None
 
     def step():
         if graph is not None:
@@ -279,10 +293,19 @@ def run_aoh(args):
     clocks.start()  # sampling runs through warm-up and the timed steps (the same steady load)
     for _ in range(args.warmup):
         step()
+    # more warm-up until nvidia-smi reports under load (2 s at most); ranks are
+    # coupled step by step, so all of them decide together and run the same steps
     t_w = time.perf_counter()
-    while not clocks.lines and time.perf_counter() - t_w < 2.0:  # until nvidia-smi reports under load
-        step()
+    for _ in range(400):  # pages are reserved for 5 * 400 extra steps
         torch.cuda.synchronize()
+        flags = torch.tensor([0 if clocks.lines else 1, 1 if time.perf_counter() - t_w >= 2.0 else 0],
+                             device=dev, dtype=torch.int32)
+        if world > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+        if flags[0].item() == 0 or flags[1].item() == 1:
+            break
+        for _ in range(5):
+            step()
     barrier()
     torch.cuda.synchronize()
     T0 = cache.kv_seq_len
@@ -376,6 +399,10 @@ def run_aoh(args):
                          "append)"}
 
     if world > 1:
+        graph = None
+        if peer is not None:
+            torch.cuda.synchronize()
+            peer.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -396,8 +423,9 @@ def run_aoh(args):
                      "avg_launch_us": round(launch_us, 3)},
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": (L_LAYERS + (1 if graph is not None else 0)) * args.steps,
-        "launch_mode": "cuda_graph+pdl" if graph is not None else "eager+pdl",
+        "gpu_launches": (L_LAYERS * (2 if peer is not None else 1) + (1 if used_graph else 0)) * args.steps,
+        "launch_mode": "cuda_graph+pdl" if used_graph else "eager+pdl",
+        "gather": None if world == 1 else ("nvlink_peer_stores" if peer is not None else "nccl_all_gather"),
         "host_enqueue_us_per_layer": round(host_us, 2),
         "clocks": clk,
         **extras,
@@ -505,6 +533,8 @@ def main():
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
     ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
     ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: output gather by peer stores from the decode kernel, or NCCL all-gather")
     args = ap.parse_args()
     _set_workload(args.context, args.layers)
     if args.warmup < 3 and args.impl == "aoh":

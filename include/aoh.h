@@ -236,6 +236,43 @@ AOH_API int aoh_partition(const uint8_t* labels, int32_t num_layers, int32_t bat
                   int32_t context, int32_t sink_size, int32_t recent_size, int32_t n_ranks,
                   int32_t* owner_out);
 
+/* ------------------------------------------------------------------------- */
+/* Output gather over NVLink (no counterpart in the reference).              */
+/* One process per GPU of one node; each rank decodes the units it owns      */
+/* (aoh_partition) and the decode kernel itself stores every finished unit's */
+/* output rows into the output region of every rank, then publishes a flag  */
+/* per (layer, unit) in every rank's flag array.  aoh_gather_wait is the     */
+/* layer boundary: it returns (on the GPU) once all units of the layer have  */
+/* arrived here.                                                             */
+/* ------------------------------------------------------------------------- */
+
+#define AOH_IPC_HANDLE_BYTES 64
+
+/* Device memory (zero-filled) that the other processes of the node can map:
+ * *dev_ptr is usable here, ipc_handle (AOH_IPC_HANDLE_BYTES) is passed to
+ * them.  Freed with aoh_shared_free. */
+AOH_API int aoh_shared_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+AOH_API int aoh_shared_free(void* dev_ptr);
+/* Map another process's aoh_shared_alloc region on the current device;
+ * unmapped with aoh_shared_close. */
+AOH_API int aoh_shared_open(const void* ipc_handle, void** dev_ptr);
+AOH_API int aoh_shared_close(void* dev_ptr);
+
+/* Attach the gather to a bf16 cache (n_ranks <= 8; n_ranks = 0 detaches).
+ * out_regions[r]: rank r's output region as mapped in this process
+ * (out_regions[rank] is this rank's own), each out_bytes long, laid out alike
+ * on every rank; flag_arrays[r]: rank r's flag array as mapped here, int32
+ * (num_layers * batch * num_kv_heads), zero-filled before the first step.
+ * While attached, aoh_attn_decode needs its `out` inside the own region and
+ * writes the same offsets in every region. */
+AOH_API int aoh_kv_set_peers(aoh_kv_cache* cache, int32_t n_ranks, int32_t rank, void* const* out_regions,
+                             size_t out_bytes, int32_t* const* flag_arrays);
+/* Stream-ordered wait until every (sequence, KV head) unit of `layer` decoded
+ * at position past_len (or the device length, AOH_PAST_LEN_DEVICE) has been
+ * stored here by its owner.  The wait is bounded: a missing peer sets the
+ * cache's device check word (aoh_kv_device_status) instead of hanging. */
+AOH_API int aoh_gather_wait(aoh_kv_cache* cache, int32_t layer, int32_t past_len, aoh_stream stream);
+
 #ifdef __cplusplus
 }
 #endif
