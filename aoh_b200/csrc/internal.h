@@ -68,6 +68,13 @@ struct aoh_kv_cache {
   char* out_regions[aoh::kMaxRanks] = {};
   size_t out_bytes = 0;
   int32_t* flag_arrays[aoh::kMaxRanks] = {};
+  // split-KV prefill scratch owned by the cache (grow-only; freed on destroy):
+  // [counters][partials]; the counters are zero between launches
+  void* prefill_ws = nullptr;
+  size_t prefill_ws_bytes = 0;
+  ~aoh_kv_cache() {
+    if (prefill_ws) cudaFree(prefill_ws);
+  }
 
   int unit(int layer, int b, int g) const { return (layer * cfg.batch + b) * cfg.num_kv_heads + g; }
   bool retrieval(int layer, int g) const { return labels[layer * cfg.num_kv_heads + g] != 0; }

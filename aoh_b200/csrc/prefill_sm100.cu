@@ -74,6 +74,8 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int q) { return q ? 128u : 0u; }    // S_q (P_q in its first 64)
 __device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 256u; }  // O_q
 constexpr int kMaxItemsP = 768;
+constexpr int kMaxSplitP = 32;                        // key-range splits of one retrieval CTA
+constexpr int kPartFloats = BM * kHeadDim + 2 * BM;  // one split's partial of one query tile: O^T, m, l
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillArgs {
@@ -81,6 +83,12 @@ struct PrefillArgs {
   CacheGeom geom;
   int layer, T, C, n_qtiles;
   float scale_log2;
+  // Split-KV: a retrieval CTA's key tiles are cut into n_split ranges (grid z);
+  // each writes a partial to ws, the last to finish (ticket in counters)
+  // combines.  ws slot = (item * n_qtiles + row block) * n_split + split.
+  int n_split;
+  float* ws;
+  int* counters;  // one per (retrieval item, row block), zero between launches
   int n_items;
   // ((b * Hq + h0) << 2) | ((heads - 1) << 1) | retrieval: heads h0 (and h0+1)
   // of one KV group; retrieval items first
@@ -257,6 +265,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   // [softmax group][buffer][column]: rows [x, y] of this CTA allowed to see the
   // key of that column of a masked tile (y < x: none)
   __shared__ char2 s_kwin[2][2][BN];
+  __shared__ int s_ticket;
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -266,9 +275,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int bh = code >> 2;
   const int b = bh / G.Hq, h0 = bh % G.Hq, g = h0 / G.grp;
   const int i0 = (a.n_qtiles - 1 - (int)blockIdx.x) * BM;  // heaviest (last) row blocks first
+  const int n_split = retr ? a.n_split : 1;
+  const int split = blockIdx.z;
+  if (split >= n_split) return;  // streaming items are not split
   TileList tl;
   tl.init(retr, a.T, a.C, i0, G);
-  const int n_tiles = tl.n_tiles;
+  // this CTA's key tiles: [t_begin, t_begin + n_tiles) of the item's list
+  const int t_begin = (int)((long long)tl.n_tiles * split / n_split);
+  const int n_tiles = (int)((long long)tl.n_tiles * (split + 1) / n_split) - t_begin;
 
   if (warp == kWarpMma) {
     tmem_alloc(&s_tmem, kTmemCols);
@@ -324,8 +338,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
     }
     auto fetch_ids = [&](int j) -> int {
-      if (j >= n_tiles || !tl.is_cache(j) || lane >= 8) return -1;
-      const int vj = j * 8 + lane;
+      const int t = t_begin + j;
+      if (j >= n_tiles || !tl.is_cache(t) || lane >= 8) return -1;
+      const int vj = t * 8 + lane;
       return vj < tl.n_pages ? bt[tl.table_index(vj)] : -1;
     };
     int ids_next = fetch_ids(0);
@@ -340,9 +355,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       __syncwarp();
       if (s_abort) break;
-      if (tl.is_cache(j)) {
+      const int t = t_begin + j;
+      if (tl.is_cache(t)) {
         const bool ok = ids >= 0 && ids < G.num_pages;
-        const bool want = lane < 8 && j * 8 + lane < tl.n_pages;
+        const bool want = lane < 8 && t * 8 + lane < tl.n_pages;
         if (kv == 0 && want && !ok) atomicOr(G.err, kErrBadPage);
         const uint32_t okm = __ballot_sync(0xffffffffu, lane < 8 && ok);
         const int id0 = __shfl_sync(0xffffffffu, ids, 0);
@@ -372,7 +388,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
       } else if (lane == 0) {
         int r0, lo, hi;
-        tl.chunk(j, &r0, &lo, &hi);
+        tl.chunk(t, &r0, &lo, &hi);
         mbar_arrive_expect_tx(&full_b[s], kTileBytes);
         tma_load_4d(dst + 0 * kKVHalf, rows_map, &full_b[s], 0, g, r0, b);
         tma_load_4d(dst + 1 * kKVHalf, rows_map, &full_b[s], 64, g, r0, b);
@@ -494,7 +510,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool full = tl.full(i);
+      const bool full = tl.full(t_begin + i);
       const char2* kw = s_kwin[q][n_masked & 1];
       if (!full) {
         // thread r resolves column r's key once for the group: the rows that
@@ -503,7 +519,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // position.  The two buffers alternate; a thread rewrites one only
         // after every thread of the group has passed the next masked tile's
         // barrier, i.e. finished reading it.
-        const int kpos = tl.key_pos(i, row);
+        const int kpos = tl.key_pos(t_begin + i, row);
         const int q0 = a.T + i0;
         int lo = max(kpos - q0, 0);
         int hi = (retr || kpos < tl.sink) ? BM - 1 : min(kpos + tl.recent - q0, BM - 1);
@@ -566,32 +582,79 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar_p_full[q]);
     }
-    // epilogue: O / l -> bf16 row of the output
-    if (!s_abort && n_tiles > 0 && mbar_wait(&bar_final, 0, G.err)) {
-      tc_fence_after();
-      float l = 0.f;
+    float l = 0.f;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float u, v;
-        f2_unpack(l2[k], u, v);
-        l += u + v;
+    for (int k = 0; k < 4; ++k) {
+      float u, v;
+      f2_unpack(l2[k], u, v);
+      l += u + v;
+    }
+    __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h0 + q) * kHeadDim;
+    auto store_row = [&](const float* o, float inv) {  // bf16 row of the output, 16 B at a time
+      if (qi >= a.C) return;
+#pragma unroll
+      for (int c = 0; c < kHeadDim / 8; ++c) {
+        uint4 w = make_uint4(pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv), pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                             pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv), pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+        reinterpret_cast<uint4*>(dst)[c] = w;
       }
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h0 + q) * kHeadDim;
+    };
+    const bool have = !s_abort && n_tiles > 0 && mbar_wait(&bar_final, 0, G.err);
+    if (have) tc_fence_after();
+    if (n_split == 1) {
+      // epilogue: O / l -> bf16 row of the output
+      if (have) {
+        float o[kHeadDim];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
+        for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + col_o(q) + 32 * c, reinterpret_cast<uint32_t*>(o) + 32 * c);
         tc_wait_ld();
-        uint32_t pk[16];
+        store_row(o, l > 0.f ? 1.f / l : 0.f);
+      }
+    } else {
+      // split epilogue: this split's partial (O^T so a warp's stores are
+      // contiguous, then m and l per row), a ticket, and the last split to
+      // arrive combines every partial of the row block
+      const int gslot = blockIdx.y * a.n_qtiles + blockIdx.x;
+      float* part = a.ws + ((size_t)(gslot * n_split + split) * 2 + q) * kPartFloats;
+      if (have) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack_bf16(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv);
-        if (qi < a.C) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
+          tc_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          for (int e = 0; e < 32; ++e) part[(32 * c + e) * BM + row] = __uint_as_float(ov[e]);
         }
+      }
+      part[BM * kHeadDim + row] = have ? m_used : -INFINITY;
+      part[BM * kHeadDim + BM + row] = have ? l : 0.f;
+      __threadfence();
+      named_bar_sync(3, nq * 128);
+      if (tid == 0) s_ticket = atomicAdd(&a.counters[gslot], 1);
+      named_bar_sync(3, nq * 128);
+      if (s_ticket == n_split - 1) {
+        __threadfence();
+        const float* p0 = a.ws + ((size_t)gslot * n_split * 2 + q) * kPartFloats;  // split s at + s * 2 * kPartFloats
+        float M = -INFINITY;
+        for (int sp = 0; sp < n_split; ++sp) {
+          const float* ps = p0 + (size_t)sp * 2 * kPartFloats;
+          if (__ldcg(ps + BM * kHeadDim + BM + row) > 0.f) M = fmaxf(M, __ldcg(ps + BM * kHeadDim + row));
+        }
+        float L = 0.f;
+        float o[kHeadDim];
+#pragma unroll
+        for (int d = 0; d < kHeadDim; ++d) o[d] = 0.f;
+        for (int sp = 0; sp < n_split; ++sp) {
+          const float* ps = p0 + (size_t)sp * 2 * kPartFloats;
+          const float ls = __ldcg(ps + BM * kHeadDim + BM + row);
+          if (!(ls > 0.f)) continue;  // an empty range: no keys for this row
+          const float w = fast_exp2(__ldcg(ps + BM * kHeadDim + row) - M);
+          L += w * ls;
+#pragma unroll
+          for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(w, __ldcg(ps + d * BM + row), o[d]);
+        }
+        store_row(o, L > 0.f ? 1.f / L : 0.f);
+        if (tid == 0) a.counters[gslot] = 0;  // ready for the next launch
       }
     }
   }
@@ -706,6 +769,55 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
         }
       }
   if (a.n_items == 0 || q_len == 0) return AOH_OK;
+  int n_retr_items = 0;
+  for (int i = 0; i < a.n_items; ++i) n_retr_items += a.item[i] & 1;
+  a.n_qtiles = (q_len + BM - 1) / BM;
+
+  // ---- split-KV plan: cut every retrieval CTA's key tiles into n_split
+  // ranges so that the heavy CTAs fill whole waves of the GPU (one CTA per SM)
+  // and short chunks still occupy every SM.  Cost model in key-tile periods:
+  // waves * (tiles per split + overhead), the overhead standing for the
+  // prologue and, when split, the partial write and combine.
+  const int heavy = n_retr_items * a.n_qtiles;
+  const int cache_tiles = ((past_len + kPage - 1) / kPage + 7) / 8;
+  const int max_tiles = cache_tiles + a.n_qtiles;  // the last row block's list
+  const int sms = std::max(1, c->num_sms);
+  int n_split = 1;
+  if (heavy > 0) {
+    double best = 0.0;
+    for (int sp = 1; sp <= kMaxSplitP; ++sp) {
+      if (sp > 1 && max_tiles / sp < 8) break;  // keep at least 8 tiles per split
+      const double waves = std::ceil((double)heavy * sp / sms);
+      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 3.0 : 1.0));
+      if (sp == 1 || cost < best * 0.97) {  // split only for a clear gain
+        best = cost;
+        n_split = sp;
+      }
+    }
+  }
+  a.n_split = n_split;
+  a.ws = nullptr;
+  a.counters = nullptr;
+  if (n_split > 1) {
+    const size_t cnt_bytes = ((size_t)heavy * sizeof(int) + 255) / 256 * 256;
+    const size_t need = cnt_bytes + (size_t)heavy * n_split * 2 * kPartFloats * sizeof(float);
+    if (c->prefill_ws_bytes < need) {
+      if (c->prefill_ws) {
+        int rc = cuda_check(cudaStreamSynchronize(st), "prefill: scratch resize");
+        if (rc) return rc;
+        cudaFree(c->prefill_ws);
+        c->prefill_ws = nullptr;
+        c->prefill_ws_bytes = 0;
+      }
+      int rc = cuda_check(cudaMalloc(&c->prefill_ws, need), "prefill: split-KV scratch");
+      if (rc) return rc;
+      c->prefill_ws_bytes = need;
+      rc = cuda_check(cudaMemsetAsync(c->prefill_ws, 0, need, st), "prefill: scratch zero fill");
+      if (rc) return rc;
+    }
+    a.counters = static_cast<int*>(c->prefill_ws);
+    a.ws = reinterpret_cast<float*>(static_cast<char*>(c->prefill_ws) + cnt_bytes);
+  }
   CUtensorMap tq, tk, tv;
   int rc = encode_rows_map(&tq, q, cf.batch, q_len, cf.num_q_heads);
   if (!rc) rc = encode_rows_map(&tk, k_new, cf.batch, q_len, cf.num_kv_heads);
@@ -716,9 +828,8 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.layer = layer;
   a.T = past_len;
   a.C = q_len;
-  a.n_qtiles = (q_len + BM - 1) / BM;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
-  dim3 grid(a.n_qtiles, a.n_items);
+  dim3 grid(a.n_qtiles, a.n_items, n_split);
   prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, c->tmap_pool_runs, a);
   return cuda_check(cudaGetLastError(), "prefill kernel launch");
 }

@@ -62,6 +62,17 @@ def test_qwen25_group7_batch2(cuda_device):
     assert max(errs.values()) <= 2e-2, errs
 
 
+@pytest.mark.parametrize("Hq,labels_row", [(8, [1, 0]), (14, [0, 1])])
+def test_split_kv_prefill_against_oracle(cuda_device, Hq, labels_row):
+    """Chunks whose retrieval CTAs are cut into key ranges (split-KV + combine):
+    a long first chunk (row blocks with fewer key tiles than splits, so some
+    ranges are empty), then short chunks over a long cache; group sizes 4 (head
+    pairs) and 7 (pairs plus a single-head CTA)."""
+    labels = np.array([labels_row], dtype=np.float64)
+    errs = _run_both("bf16", Hq, 2, labels, [3000, 2500, 256, 200, 129], 2, 128, 256, seed=24)
+    assert max(errs.values()) <= 2e-2, errs
+
+
 @pytest.mark.parametrize("sink,recent", [(0, 0), (0, 40), (7, 0), (16, 16), (130, 250)])
 def test_window_edge_cases(cuda_device, sink, recent):
     labels = np.array([[0, 1]], dtype=np.float64)
