@@ -59,7 +59,7 @@ constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // warp 11 only completes 
 // threads may hold); warpgroup 2 (loads, MMA issue) then gives registers
 // back and the two softmax warpgroups take them.  The shares must fit the
 // launch total: 2 * 128 * kRegsSoftmax + 128 * kRegsOther <= 384 * kRegsLaunch.
-constexpr int kRegsLaunch = 168, kRegsSoftmax = 208, kRegsOther = 88;
+constexpr int kRegsLaunch = 168, kRegsSoftmax = 216, kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kPThreads * kRegsLaunch, "register split");
 constexpr int kQTile = 2 * BM * 128;        // one query tile: [half][row][128 B]
 constexpr int kKVHalf = BN * 128;           // one 64-dim half of K or V for a key tile
@@ -83,10 +83,14 @@ struct PrefillArgs {
   CacheGeom geom;
   int layer, T, C, n_qtiles;
   float scale_log2;
-  // Split-KV: a retrieval CTA's key tiles are cut into n_split ranges (grid z);
-  // each writes a partial to ws, the last to finish (ticket in counters)
-  // combines.  ws slot = (item * n_qtiles + row block) * n_split + split.
+  // Split-KV: a retrieval CTA's key tiles are cut into n_split ranges; each
+  // writes a partial to ws, the last to finish (ticket in counters) combines.
+  // ws slot = (item * n_qtiles + row block) * n_split + split.
+  // Grid (1-D): first every (row block, retrieval item, split) -- row blocks
+  // fastest, so neighbouring CTAs read the same key tiles -- then every
+  // (row block, streaming item): short CTAs that fill the last wave's tail.
   int n_split;
+  int n_retr_items;
   float* ws;
   int* counters;  // one per (retrieval item, row block), zero between launches
   int n_items;
@@ -269,15 +273,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int code = a.item[blockIdx.y];
+  const int heavy = a.n_retr_items * a.n_qtiles;
+  int item_idx, qtile, split;
+  if ((int)blockIdx.x < heavy * a.n_split) {
+    qtile = blockIdx.x % a.n_qtiles;
+    item_idx = (blockIdx.x / a.n_qtiles) % a.n_retr_items;
+    split = blockIdx.x / heavy;
+  } else {
+    const int r = blockIdx.x - heavy * a.n_split;
+    qtile = r % a.n_qtiles;
+    item_idx = a.n_retr_items + r / a.n_qtiles;
+    split = 0;
+  }
+  const int code = a.item[item_idx];
   const bool retr = code & 1;
   const int nq = ((code >> 1) & 1) + 1;  // query tiles in this CTA
   const int bh = code >> 2;
   const int b = bh / G.Hq, h0 = bh % G.Hq, g = h0 / G.grp;
-  const int i0 = (a.n_qtiles - 1 - (int)blockIdx.x) * BM;  // heaviest (last) row blocks first
+  const int i0 = (a.n_qtiles - 1 - qtile) * BM;  // heaviest (last) row blocks first
   const int n_split = retr ? a.n_split : 1;
-  const int split = blockIdx.z;
-  if (split >= n_split) return;  // streaming items are not split
   TileList tl;
   tl.init(retr, a.T, a.C, i0, G);
   // this CTA's key tiles: [t_begin, t_begin + n_tiles) of the item's list
@@ -614,7 +628,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       // split epilogue: this split's partial (O^T so a warp's stores are
       // contiguous, then m and l per row), a ticket, and the last split to
       // arrive combines every partial of the row block
-      const int gslot = blockIdx.y * a.n_qtiles + blockIdx.x;
+      const int gslot = item_idx * a.n_qtiles + qtile;
       float* part = a.ws + ((size_t)(gslot * n_split + split) * 2 + q) * kPartFloats;
       if (have) {
 #pragma unroll
@@ -779,8 +793,11 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   // waves * (tiles per split + overhead), the overhead standing for the
   // prologue and, when split, the partial write and combine.
   const int heavy = n_retr_items * a.n_qtiles;
+  const int light = (a.n_items - n_retr_items) * a.n_qtiles;
   const int cache_tiles = ((past_len + kPage - 1) / kPage + 7) / 8;
   const int max_tiles = cache_tiles + a.n_qtiles;  // the last row block's list
+  // a streaming CTA's list: sink + ring pages, and the window's new rows
+  const int light_tiles = (c->sink_pages + c->ring_pages + 7) / 8 + (cf.sink_size + cf.recent_size) / BM + 2;
   const int sms = std::max(1, c->num_sms);
   int n_split = 1;
   if (heavy > 0) {
@@ -788,7 +805,11 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     for (int sp = 1; sp <= kMaxSplitP; ++sp) {
       if (sp > 1 && max_tiles / sp < 8) break;  // keep at least 8 tiles per split
       const double waves = std::ceil((double)heavy * sp / sms);
-      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 3.0 : 1.0));
+      // streaming CTAs run after the split CTAs: in the last wave's free slots
+      // if they fit, else as extra short waves
+      const double spare = waves * sms - (double)heavy * sp;
+      const double extra = light > spare ? std::ceil((light - spare) / sms) * light_tiles : 0.0;
+      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 3.0 : 1.0)) + extra;
       if (sp == 1 || cost < best * 0.97) {  // split only for a clear gain
         best = cost;
         n_split = sp;
@@ -796,6 +817,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     }
   }
   a.n_split = n_split;
+  a.n_retr_items = n_retr_items;
   a.ws = nullptr;
   a.counters = nullptr;
   if (n_split > 1) {
@@ -829,7 +851,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.T = past_len;
   a.C = q_len;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
-  dim3 grid(a.n_qtiles, a.n_items, n_split);
+  dim3 grid(heavy * n_split + light, 1, 1);
   prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, c->tmap_pool_runs, a);
   return cuda_check(cudaGetLastError(), "prefill kernel launch");
 }

@@ -387,7 +387,12 @@ def run_aoh(args):
     extras = {}
     if rank == 0 and world == 1:
         if not args.no_prefill:
-            extras["prefill"] = prefill_sample(torch, dev, bf16_peak)
+            extras["prefill"] = {
+                "workload": "qwen25_7b_chunked_prefill_64k (28 layers, 28/4 heads, 2/4 streaming, bf16)",
+                "chunk_4096": prefill_full(torch, dev, bf16_peak, 4096),
+                "chunk_256": prefill_full(torch, dev, bf16_peak, 256),
+                "kernel_sample": prefill_sample(torch, dev, bf16_peak),
+            }
         if not args.no_classifier:
             extras["labels_exact"] = classifier_check(torch, dev)
     cpu = None
@@ -471,6 +476,56 @@ def prefill_sample(torch, dev, bf16_peak):
             "flops": flops}
 
 
+def prefill_full(torch, dev, bf16_peak, chunk: int, context: int = 65536, layers: int = 28):
+    """Chunked prefill to ``context`` tokens through every layer: Qwen2.5-7B
+    shapes (28 query / 4 KV heads, head_dim 128), bf16, 2 of 4 KV heads streaming
+    per layer (seeded), sink 128, window 256, q/k/v ~ N(0,1) generated once per
+    layer and reused for every chunk (values do not change the work).  The whole
+    prefill runs twice: the first pass warms up (kernel attributes, split-KV
+    scratch sized for every chunk), the second is timed with CUDA events.  Flops
+    count only masked-in (query, key) pairs."""
+    from aoh_b200 import AoHKVCache, aoh_attention
+    from aoh_b200 import synthetic as syn
+    from aoh_b200.metrics import attention_flops
+    Hq, Gq, sink, recent = 28, 4, 128, 256
+    grp = Hq // Gq
+    labels = syn.labels_uniform(31, layers, Gq, 2)
+    cache = AoHKVCache(labels, Hq, batch=1, sink_size=sink, recent_size=recent, max_context=context,
+                       dtype=torch.bfloat16, device=dev, reserve_all=True)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    qs = [torch.randn((1, chunk, Hq, D), generator=gen, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    ks = [torch.randn((1, chunk, Gq, D), generator=gen, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn((1, chunk, Gq, D), generator=gen, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    out = torch.empty_like(qs[0])
+
+    def run():
+        cache.kv_seq_len = 0
+        for _ in range(0, context, chunk):
+            for l in range(layers):
+                aoh_attention(cache, l, qs[l], ks[l], vs[l], out=out)
+
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    assert cache.device_status() == 0, "device-side check tripped"
+    sec = e0.elapsed_time(e1) / 1000.0
+    flops = 0
+    for start in range(0, context, chunk):
+        f_ret = attention_flops(chunk, start, True, sink, recent)
+        f_str = attention_flops(chunk, start, False, sink, recent)
+        for l in range(layers):
+            n_ret = int((labels[l] >= 0.5).sum())
+            flops += grp * (n_ret * f_ret + (Gq - n_ret) * f_str)
+    tf = flops / sec / 1e12
+    cache.close()
+    return {"chunk": chunk, "tflops": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4),
+            "seconds": round(sec, 4), "flops": flops, "calls": layers * (context // chunk)}
+
+
 def classifier_check(torch, dev):
     """AoH classifier on seeded Qwen2.5-7B-shaped projections (28 layers, 28/4
     heads, hidden 3584, bf16): GPU effective ranks -> labels vs the reference's
@@ -531,6 +586,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-classifier", action="store_true")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
+    ap.add_argument("--prefill-full", type=int, default=0, metavar="CHUNK",
+                    help="only the full 64K chunked prefill at this chunk size")
     ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
     ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
@@ -547,6 +604,13 @@ def main():
         torch.cuda.set_device(0)
         _, bf16_peak, _ = measured_peaks()
         print(json.dumps({"prefill": prefill_sample(torch, torch.device("cuda", 0), bf16_peak)}), flush=True)
+        return 0
+    if args.prefill_full:
+        import torch
+        torch.cuda.set_device(0)
+        _, bf16_peak, _ = measured_peaks()
+        print(json.dumps({"prefill": prefill_full(torch, torch.device("cuda", 0), bf16_peak, args.prefill_full)}),
+              flush=True)
         return 0
     return run_aoh(args)
 
