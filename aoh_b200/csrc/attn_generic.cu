@@ -238,8 +238,15 @@ struct AppendArgs {
 };
 
 // One warp per (token, unit): writes the K and V rows of position T + i.
+// Launched with programmatic dependent launch after the attention kernel of
+// the same call: it waits for that kernel (whose CTAs still read the ring
+// slots this overwrites) before writing, and only then lets the next kernel
+// in the stream start, so a starting kernel never overlaps anything older
+// than its immediate predecessor.
 template <typename T>
 __global__ void __launch_bounds__(128) append_kernel(const AppendArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const CacheGeom& G = a.geom;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * 4 + warp;
@@ -354,12 +361,19 @@ int launch_append(aoh_kv_cache* c, int layer, int past_len, int q_len, const voi
   a.layer = layer;
   a.T = past_len;
   a.C = q_len;
-  dim3 grid((q_len + 3) / 4, a.n_units);
+  c->last_write_layer = layer;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((q_len + 3) / 4, a.n_units);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (c->cfg.dtype == AOH_F32)
-    append_kernel<float><<<grid, 128, 0, st>>>(a);
-  else
-    append_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a);
-  return cuda_check(cudaGetLastError(), "append kernel launch");
+    return cuda_check(cudaLaunchKernelEx(&cfg, append_kernel<float>, a), "append kernel launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, append_kernel<__nv_bfloat16>, a), "append kernel launch");
 }
 
 }  // namespace aoh

@@ -80,6 +80,10 @@ struct DecodeArgs {
   // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
   // bytes for every rank r (its output region as mapped here), then the flag
   // (layer, unit) of every rank's flag array is set to T + 1
+  // 0: the kernel before this one in the stream wrote this layer's pages
+  // (e.g. a prefill chunk's append), so no page is streamed before waiting
+  // for it; 1: only the page of position T-1 may still be in flight
+  int prefetch;
   int n_ranks;
   long long out_delta[kMaxRanks];
   int32_t* flags[kMaxRanks];
@@ -243,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued = 0;
     const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
     const int hot_vj = uv.last_written_page();
+    if (!a.prefetch) griddep_wait();
     int nxt = -1;
     if (lane < nloc) nxt = bt[uv.table_index(v0 + lane)];
     for (int base = 0; base < nloc; base += 32) {
@@ -763,6 +768,8 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   }
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(grid, st, attr, true);
+  a.prefetch = c->last_write_layer != layer ? 1 : 0;
+  c->last_write_layer = layer;  // the kernel appends the new token to this layer
   return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");
 }
 

@@ -70,6 +70,10 @@ struct aoh_kv_cache {
   int32_t* flag_arrays[aoh::kMaxRanks] = {};
   // split-KV prefill scratch owned by the cache (grow-only; freed on destroy):
   // [counters][partials]; the counters are zero between launches
+  // layer whose pages the last stream-ordered write kernel (append, decode
+  // append) touched; a following prefill of another layer may prefetch its
+  // pages before waiting for that kernel
+  int last_write_layer = -1;
   void* prefill_ws = nullptr;
   size_t prefill_ws_bytes = 0;
   ~aoh_kv_cache() {

@@ -91,6 +91,9 @@ struct PrefillArgs {
   // (row block, streaming item): short CTAs that fill the last wave's tail.
   int n_split;
   int n_retr_items;
+  // 1: the kernel before this one in the stream wrote another layer's pages,
+  // so the first cache tiles may be fetched before waiting for it
+  int prefetch;
   float* ws;
   int* counters;  // one per (retrieval item, row block), zero between launches
   int n_items;
@@ -344,13 +347,31 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const CUtensorMap* rows_map = kv ? &tm_v : &tm_k;
     const int32_t* bt = G.block_table + G.unit_offset[(a.layer * G.B + b) * G.G + g];
     const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
-    if (kv == 0 && lane == 0) {
-      mbar_arrive_expect_tx(&bar_q, nq * kQTile);
-      for (int q = 0; q < nq; ++q) {
-        tma_load_4d(sQ + q * kQTile, &tm_q, &bar_q, 0, h0 + q, i0, b);
-        tma_load_4d(sQ + q * kQTile + kQTile / 2, &tm_q, &bar_q, 64, h0 + q, i0, b);
+    // Programmatic dependent launch: this kernel may start while the previous
+    // kernel in the stream finishes.  q and this call's new rows (and, when
+    // that kernel wrote this layer, the cache pages) are read only after
+    // griddepcontrol.wait; the first cache tiles of the ring may be fetched
+    // before it.  The dependents are released only after the wait, so a
+    // kernel never overlaps anything but its immediate predecessor.
+    int n_pre = 0;
+    if (a.prefetch)
+      while (n_pre < nst && n_pre < n_tiles && tl.is_cache(t_begin + n_pre)) ++n_pre;
+    bool waited = false;
+    auto wait_prev = [&]() {
+      griddep_wait();
+      waited = true;
+      if (kv == 0) {
+        griddep_launch_dependents();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_q, nq * kQTile);
+          for (int q = 0; q < nq; ++q) {
+            tma_load_4d(sQ + q * kQTile, &tm_q, &bar_q, 0, h0 + q, i0, b);
+            tma_load_4d(sQ + q * kQTile + kQTile / 2, &tm_q, &bar_q, 64, h0 + q, i0, b);
+          }
+        }
       }
-    }
+    };
+    if (n_pre == 0) wait_prev();
     auto fetch_ids = [&](int j) -> int {
       const int t = t_begin + j;
       if (j >= n_tiles || !tl.is_cache(t) || lane >= 8) return -1;
@@ -360,6 +381,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     int ids_next = fetch_ids(0);
     int issued = 0;
     for (int j = 0; j < n_tiles; ++j) {
+      if (j == n_pre && !waited) wait_prev();
       const int ids = ids_next;
       ids_next = fetch_ids(j + 1);  // page ids of the next tile, in flight during this one
       const int s = j % nst, rnd = j / nst;
@@ -410,6 +432,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       issued = j + 1;
       __syncwarp();
     }
+    if (!waited) wait_prev();
     // nothing this CTA issued may still be landing when it exits
     if (lane == 0) {
       if (kv == 0) mbar_wait(&bar_q, 0, G.err);
@@ -818,6 +841,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   }
   a.n_split = n_split;
   a.n_retr_items = n_retr_items;
+  a.prefetch = c->last_write_layer != layer ? 1 : 0;
   a.ws = nullptr;
   a.counters = nullptr;
   if (n_split > 1) {
@@ -851,9 +875,18 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.T = past_len;
   a.C = q_len;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
-  dim3 grid(heavy * n_split + light, 1, 1);
-  prefill_bf16_kernel<<<grid, kPThreads, kPSmem, st>>>(tq, tk, tv, c->tmap_pool_runs, a);
-  return cuda_check(cudaGetLastError(), "prefill kernel launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(heavy * n_split + light, 1, 1);
+  cfg.blockDim = dim3(kPThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, prefill_bf16_kernel, tq, tk, tv, c->tmap_pool_runs, a),
+                    "prefill kernel launch");
 }
 
 }  // namespace aoh
