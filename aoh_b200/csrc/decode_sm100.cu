@@ -101,13 +101,15 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, __nv_bfloat16* p,
 }
 
 // The unit's rows are stored everywhere and the caller's barrier ordered every
-// writer before this thread: the release stores (system scope, cumulative over
-// what the barrier ordered before them) publish (layer, unit) = T + 1 to every
-// rank.
+// writer before this thread: one system-scope fence (cumulative over what the
+// barrier ordered before it) followed by relaxed system-scope stores is the
+// release that publishes (layer, unit) = T + 1 to every rank -- one fence for
+// all ranks instead of one per release store.
 __device__ __forceinline__ void publish_unit(const DecodeArgs& a, int bg, int T) {
   const int idx = a.layer * a.geom.B * a.geom.G + bg;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   for (int r = 0; r < a.n_ranks; ++r)
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(a.flags[r] + idx), "r"(T + 1) : "memory");
+    asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(a.flags[r] + idx), "r"(T + 1) : "memory");
 }
 
 // A unit's compact page list: retrieval pages 0..ceil(T/16)-1; streaming the
