@@ -48,6 +48,8 @@ L_LAYERS, HQ, G, D, T_CTX = 32, 32, 8, 128, 131072
 N_STREAM, SINK, RECENT, KV_SCALE, SEED = 6, 128, 256, 0.5, 0
 METRIC = "decode attn us/layer @128K"
 WORKLOAD = "llama31_8b_decode_128k"
+BATCH_FIXED = 0      # > 0: strong scaling with this many sequences (else one per GPU)
+SKEWED_LABELS = False
 
 
 # ----------------------------------------------------------------------------
@@ -208,8 +210,8 @@ def run_aoh(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    B = world  # one 128K sequence per GPU
-    labels = syn.labels_uniform(SEED, L_LAYERS, G, N_STREAM)
+    B = BATCH_FIXED or world  # default: one sequence per GPU (weak scaling)
+    labels = (syn.labels_skewed if SKEWED_LABELS else syn.labels_uniform)(SEED, L_LAYERS, G, N_STREAM)
     n_ret_layer = int((labels[0] >= 0.5).sum())
     # partition (sequence, KV head) units over ranks
     owner = np.zeros((L_LAYERS, B, G), dtype=np.int32)
@@ -415,7 +417,7 @@ def run_aoh(args):
     line = {
         "metric": METRIC, "value": round(us_layer_seq, 3), "unit": "us/layer", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong" if BATCH_FIXED else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "layers": L_LAYERS, "sequences": B, "context": T_CTX,
                    "q_heads": HQ, "kv_heads": G, "head_dim": D, "page": 16,
                    "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT,
@@ -568,8 +570,15 @@ def classifier_check(torch, dev):
     return res
 
 
-def _set_workload(context: int, layers: int) -> None:
-    global T_CTX, L_LAYERS, WORKLOAD
+def _set_workload(context: int, layers: int, name: str = "llama31_8b_decode_128k") -> None:
+    global T_CTX, L_LAYERS, WORKLOAD, BATCH_FIXED, SKEWED_LABELS, METRIC
+    if name == "qwen3_8b_decode_256k_b8":
+        # batched long decode across GPUs: Qwen3-8B attention shapes (32 query /
+        # 8 KV heads), 36 layers, 8 sequences of 262144 tokens, 6/8 streaming,
+        # retrieval heads clustered in KV groups 0-1; strong scaling
+        T_CTX, L_LAYERS, BATCH_FIXED, SKEWED_LABELS = 262144, 36, 8, True
+        WORKLOAD, METRIC = name, "decode attn us/(layer*sequence) @256K batch 8"
+        return
     if context != T_CTX or layers != L_LAYERS:
         T_CTX, L_LAYERS = context, layers
         WORKLOAD = f"llama31_8b_decode_{T_CTX}_ctx_{L_LAYERS}_layers"
@@ -590,10 +599,13 @@ def main():
                     help="only the full 64K chunked prefill at this chunk size")
     ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
     ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
+    ap.add_argument("--workload", choices=["llama31_8b_decode_128k", "qwen3_8b_decode_256k_b8"],
+                    default="llama31_8b_decode_128k",
+                    help="decode workload; the second is the 8-sequence 256K strong-scaling case")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: output gather by peer stores from the decode kernel, or NCCL all-gather")
     args = ap.parse_args()
-    _set_workload(args.context, args.layers)
+    _set_workload(args.context, args.layers, args.workload)
     if args.warmup < 3 and args.impl == "aoh":
         print("note: --warmup raised to 3", file=sys.stderr)
         args.warmup = 3
