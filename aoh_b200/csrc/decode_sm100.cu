@@ -57,6 +57,7 @@ constexpr int kOPitch = kHeadDim + 4;  // padded row of the warp-merge scratch
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
 constexpr int kCounterBytes = kMaxUnits * 4;
 constexpr int kCluster = 8;
+static_assert(kMaxGrp * kHeadDim / kCluster <= kThreads, "a cluster CTA's output slice is one element per thread");
 
 struct DecodePlan {
   int n_units;
@@ -534,17 +535,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[kMaxGrp * kHeadDim + kMaxGrp + qq] = L;
       }
     }
-    __threadfence();
+    // The cluster barrier orders every CTA's partial stores before rank 0's
+    // ticket; the ticket is an acq_rel atomic at GPU scope, cumulative over
+    // them (release) and, for the last cluster, over every other cluster's
+    // partial (acquire), which the next cluster barrier extends to its CTAs.
     cluster_sync_all();  // the cluster's partial is complete; no DSMEM reads after this
     if (rank == 0 && tid == 0) {
-      const int ticket = atomicAdd(&a.counters[u], 1);
+      int ticket;
+      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(ticket) : "l"(&a.counters[u]) : "memory");
       const uint32_t last = ticket == nk - 1;
       for (int c = 0; c < kCluster; ++c) st_dsmem_u32(mapa_shared((const void*)&s_last, c), last);
     }
     cluster_sync_all();
     if (!s_last) return;
     // ============ last cluster of the unit: combine its nk partials, 1/8 of outputs per CTA ============
-    __threadfence();
+    // this thread's element of the first 16 partials, in flight while the weights are formed
+    // (a CTA's slice is at most kThreads elements: one per thread)
+    const int e_mine = e_lo + tid;
+    float v_first[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      v_first[j] = (e_mine < e_hi && j < nk) ? __ldcg(parts + e_mine + (size_t)j * kPartialFloats) : 0.f;
     // weights w[k][q] = exp2(m_k - M_q) / L_q in shared memory (the stage ring is free)
     float* sw = reinterpret_cast<float*>(smem);      // [nk][kMaxGrp]
     float* sml = sw + kMaxSplit / kCluster * kMaxGrp;  // [nk][kMaxGrp][2] raw (m, l)
@@ -574,11 +585,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = lane; k < nk; k += 32) sw[k * kMaxGrp + qq] *= inv;
     }
     __syncthreads();
-    for (int e = e_lo + tid; e < e_hi; e += kThreads) {
+    if (e_mine < e_hi) {
+      const int e = e_mine;
       const int qq = e >> 7;
       const float* po = parts + e;  // partial k's output e at po[k * kPartialFloats]
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      int k = 0;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < nk) acc[j & 3] += v_first[j] * sw[j * kMaxGrp + qq];
+      int k = 16;
       for (; k + 16 <= nk; k += 16) {
         float v[16];
 #pragma unroll
