@@ -251,6 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* pool = static_cast<const uint8_t*>(G.pool);
     const int hot_vj = uv.last_written_page();
     if (!a.prefetch) griddep_wait();
+    // Pages are read once per step: stream them with L2 evict-first, so they
+    // do not push out lines that are reused (tables, q, workspace, outputs).
+    const uint64_t pol_stream = l2_policy_evict_first();
     int nxt = -1;
     if (lane < nloc) nxt = bt[uv.table_index(v0 + lane)];
     for (int base = 0; base < nloc; base += 32) {
@@ -271,7 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (pid >= 0 && pid < G.num_pages) {
             s_bad[st] = 0;
             mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
-            bulk_load(smem + st * kStageBytes, pool + (size_t)pid * kPageBf16Bytes, kStageBytes, &full_bar[st]);
+            bulk_load_hint(smem + st * kStageBytes, pool + (size_t)pid * kPageBf16Bytes, kStageBytes, &full_bar[st],
+                           pol_stream);
             issued = i + 1;
           } else {
             atomicOr(G.err, kErrBadPage);
