@@ -2,6 +2,7 @@
 head classifier, with the API of ernie-research/AoH.
 
     from aoh_b200 import AoHClassifier, AoHKVCache, aoh_attention
+    from aoh_b200 import patch_aoh_model   # HF models (transformers), as the reference's
 
 The CUDA kernels live in libaoh.so (built in-tree by ``python -m aoh_b200.build``)
 behind the C ABI of include/aoh.h.
@@ -11,6 +12,16 @@ from .cache import AoHKVCache, pages_needed
 from .classifier import AoHClassifier, compute_all_eff_ranks, compute_eff_rank, label_margins
 from .io import load_results, save_results
 
+
+
+def __getattr__(name):
+    # HF integration (imports transformers): loaded on first use
+    if name in ("patch_aoh_model", "AoHModelCache"):
+        from . import hf
+        return getattr(hf, name)
+    raise AttributeError(f"module 'aoh_b200' has no attribute {name!r}")
+
+
 __all__ = [
     "AoHClassifier",
     "AoHKVCache",
@@ -18,6 +29,7 @@ __all__ = [
     "compute_all_eff_ranks",
     "compute_eff_rank",
     "label_margins",
+    "patch_aoh_model",
     "load_results",
     "pages_needed",
     "save_results",
