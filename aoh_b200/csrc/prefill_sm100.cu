@@ -20,26 +20,36 @@
 // with the 128-byte swizzle).  Streaming heads list only their sink and ring
 // pages and the new rows inside the window.
 //
-// Warps (384 threads; registers are moved from warpgroup 2 to the softmax
-// warpgroups with setmaxnreg):
+// Work split: retrieval CTAs may be cut into key ranges (split-KV) so short
+// chunks fill the GPU; each range writes an fp32 partial and the last to
+// finish combines (ticket).  The 1-D grid lists the split CTAs first and the
+// short streaming CTAs last, so the latter fill the final wave.
+//
+// Warps (384 threads; setmaxnreg moves registers from warpgroup 2, 72 per
+// thread, to the softmax warpgroups, 216 per thread):
 //   warp 8      K producer: both Q tiles once, then K tiles into a 2-stage ring.
 //   warp 10     V producer: V tiles into a 3-stage ring (mbarriers); the two
 //               rings are released at different times, so they are fed by
-//               separate warps and neither waits on the other.
-//   warp 9      allocates all 512 TMEM columns; lane 0 issues the MMAs, per
-//               key tile i:  S0 = Q0 K_i^T,  O1 += P1(i-1) V_{i-1},
-//               S1 = Q1 K_i^T,  O0 += P0(i) V_i   (tcgen05, SS for QK^T with
-//               K-major operands, TS for PV with P read from TMEM and V
-//               MN-major).  tcgen05.mma runs in issue order, so P_q (which
-//               overwrites the first 64 columns of S_q in place) is consumed
-//               before the next S_q is written, and O_q is final for tile
-//               i-1 whenever S_q(i) is.
+//               separate warps and neither waits on the other.  Under
+//               programmatic dependent launch the producers may fetch their
+//               first cache tiles before waiting for the previous kernel;
+//               q and this call's new rows only after.
+//   warp 9      allocates all 512 TMEM columns and issues the MMAs (the whole
+//               warp runs the loop, lane 0 issues), per key tile i:
+//               S0 = Q0 K_i^T,  O1 += P1(i-1) V_{i-1},  S1 = Q1 K_i^T,
+//               O0 += P0(i) V_i   (tcgen05, SS for QK^T with K-major operands,
+//               TS for PV with P read from TMEM and V MN-major).  tcgen05.mma
+//               runs in issue order, so P_q (which overwrites the first 64
+//               columns of S_q in place) is consumed before the next S_q is
+//               written, and O_q is final for tile i-1 whenever S_q(i) is.
 //   warps 0-3   softmax of tile 0, warps 4-7 of tile 1: thread r owns row r
-//               (TMEM lane r; warp w reaches lanes [32 (w % 4), +32)).  Pass 1 reads S in 32-column chunks for the row
-//               max; pass 2 re-reads them, writes P = 2^(s*scale - m) as bf16
-//               over the consumed columns, and sums the row.  The reference max
-//               is raised only when a tile exceeds it by more than 2^8 (then O
-//               is rescaled in TMEM).  The epilogue writes O / l.
+//               (TMEM lane r; warp w reaches lanes [32 (w % 4), +32)).  One
+//               TMEM read brings the whole S row into registers; the row max
+//               (three-input max chains), P = 2^(s*scale - m) as bf16 written
+//               over S (packed f32x2 math, part of the exponentials on the
+//               FMA pipe) and the row sum follow.  The reference max is raised
+//               only when a tile exceeds it by more than 2^8 (then O is
+//               rescaled in TMEM).  The epilogue writes O / l (or a partial).
 // TMEM columns: S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512).
 #include <cfloat>
 #include <type_traits>
