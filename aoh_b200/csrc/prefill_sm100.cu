@@ -107,8 +107,11 @@ struct PrefillArgs {
   float* ws;
   int* counters;  // one per (retrieval item, row block), zero between launches
   int n_items;
-  // ((b * Hq + h0) << 2) | ((heads - 1) << 1) | retrieval: heads h0 (and h0+1)
-  // of one KV group; retrieval items first
+  // ((b * Hq + h0) << 3) | (row_pair << 2) | ((tiles - 1) << 1) | retrieval;
+  // retrieval items first.  tiles = 2: heads h0 and h0+1 of one KV group over
+  // the same rows, or (row_pair, retrieval only) head h0 over two adjacent row
+  // blocks -- the leftover head of an odd group; its slots pair row blocks
+  // (n-1-2s, n-2-2s), so slots s >= ceil(n/2) have no work.
   int item[kMaxItemsP];
 };
 
@@ -196,13 +199,14 @@ struct TileList {
     const int row = r0 + c;
     return (row >= lo && row < hi) ? T + row : -1;
   }
-  // true when every (query row of this CTA, key of tile j) pair is allowed
-  __device__ __forceinline__ bool full(int j) const {
+  // true when every (query row of the block starting at row i0q <= i0, key of
+  // tile j) pair is allowed
+  __device__ __forceinline__ bool full_for(int j, int i0q) const {
     if (!retr) return false;
     if (is_cache(j)) return (j * 8 + 8) * kPage <= T;
     int r0, lo, hi;
     chunk(j, &r0, &lo, &hi);
-    return r0 >= lo && r0 + BN <= hi && r0 + BN - 1 <= i0;
+    return r0 >= lo && r0 + BN <= min(hi, min(C, i0q + BM)) && r0 + BN - 1 <= i0q;
   }
 };
 
@@ -300,10 +304,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
   const int code = a.item[item_idx];
   const bool retr = code & 1;
-  const int nq = ((code >> 1) & 1) + 1;  // query tiles in this CTA
-  const int bh = code >> 2;
+  const bool row_pair = (code >> 2) & 1;
+  int nq = ((code >> 1) & 1) + 1;  // query tiles in this CTA
+  const int bh = code >> 3;
   const int b = bh / G.Hq, h0 = bh % G.Hq, g = h0 / G.grp;
-  const int i0 = (a.n_qtiles - 1 - qtile) * BM;  // heaviest (last) row blocks first
+  int i0 = (a.n_qtiles - 1 - qtile) * BM;  // heaviest (last) row blocks first
+  int i0b = i0;                            // first row of tile 1
+  if (row_pair) {
+    const int rb = a.n_qtiles - 1 - 2 * qtile;  // the later row block of the pair
+    if (rb < 0) return;                         // a slot past the pairs: no work
+    i0 = rb * BM;
+    i0b = (rb - 1) * BM;
+    nq = rb >= 1 ? 2 : 1;
+  }
+  // tile q: head and first row (a row pair's tiles share the head; the later
+  // block's key tiles include the earlier block's, which masks the extra one)
+  auto q_head = [&](int q) { return row_pair ? h0 : h0 + q; };
+  auto q_row0 = [&](int q) { return q ? i0b : i0; };
   const int n_split = retr ? a.n_split : 1;
   TileList tl;
   tl.init(retr, a.T, a.C, i0, G);
@@ -375,8 +392,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (lane == 0) {
           mbar_arrive_expect_tx(&bar_q, nq * kQTile);
           for (int q = 0; q < nq; ++q) {
-            tma_load_4d(sQ + q * kQTile, &tm_q, &bar_q, 0, h0 + q, i0, b);
-            tma_load_4d(sQ + q * kQTile + kQTile / 2, &tm_q, &bar_q, 64, h0 + q, i0, b);
+            tma_load_4d(sQ + q * kQTile, &tm_q, &bar_q, 0, q_head(q), q_row0(q), b);
+            tma_load_4d(sQ + q * kQTile + kQTile / 2, &tm_q, &bar_q, 64, q_head(q), q_row0(q), b);
           }
         }
       }
@@ -514,7 +531,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int row = 32 * quarter + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
     const uint32_t s_col = lane_base + col_s(q);
-    const int qi = i0 + row;
+    const int i0q = q_row0(q);
+    const int qi = i0q + row;
     const float sl2 = a.scale_log2;
     float m_used = -INFINITY;
     int n_masked = 0;  // masked tiles seen so far: picks the key-position buffer
@@ -557,7 +575,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool full = tl.full(t_begin + i);
+      const bool full = tl.full_for(t_begin + i, i0q);
       const char2* kw = s_kwin[q][n_masked & 1];
       if (!full) {
         // thread r resolves column r's key once for the group: the rows that
@@ -567,7 +585,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // after every thread of the group has passed the next masked tile's
         // barrier, i.e. finished reading it.
         const int kpos = tl.key_pos(t_begin + i, row);
-        const int q0 = a.T + i0;
+        const int q0 = a.T + i0q;
         int lo = max(kpos - q0, 0);
         int hi = (retr || kpos < tl.sink) ? BM - 1 : min(kpos + tl.recent - q0, BM - 1);
         if (kpos < 0 || lo > BM - 1 || hi < lo) {
@@ -636,7 +654,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       f2_unpack(l2[k], u, v);
       l += u + v;
     }
-    __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + h0 + q) * kHeadDim;
+    __nv_bfloat16* dst = a.out + (((size_t)b * a.C + qi) * G.Hq + q_head(q)) * kHeadDim;
     auto store_row = [&](const float* o, float inv) {  // bf16 row of the output, 16 B at a time
       if (qi >= a.C) return;
 #pragma unroll
@@ -812,7 +830,10 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
             return fail(AOH_ERR_UNSUPPORTED, "prefill: more than %d (sequence, head pair) items", kMaxItemsP);
           const int h0 = g * grp + j;
           const int heads = grp - j >= 2 ? 2 : 1;
-          a.item[a.n_items++] = ((b * cf.num_q_heads + h0) << 2) | ((heads - 1) << 1) | (r ? 1 : 0);
+          // a retrieval group's leftover head pairs two row blocks instead
+          const int row_pair = (heads == 1 && r && q_len > BM) ? 1 : 0;
+          a.item[a.n_items++] = ((b * cf.num_q_heads + h0) << 3) | (row_pair << 2) |
+                                ((heads - 1 + row_pair) << 1) | (r ? 1 : 0);
         }
       }
   if (a.n_items == 0 || q_len == 0) return AOH_OK;
@@ -825,7 +846,10 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   // and short chunks still occupy every SM.  Cost model in key-tile periods:
   // waves * (tiles per split + overhead), the overhead standing for the
   // prologue and, when split, the partial write and combine.
-  const int heavy = n_retr_items * a.n_qtiles;
+  const int heavy = n_retr_items * a.n_qtiles;  // grid slots (row-pair items leave half empty)
+  int heavy_live = 0;
+  for (int i = 0; i < n_retr_items; ++i)
+    heavy_live += (a.item[i] >> 2) & 1 ? (a.n_qtiles + 1) / 2 : a.n_qtiles;
   const int light = (a.n_items - n_retr_items) * a.n_qtiles;
   const int cache_tiles = ((past_len + kPage - 1) / kPage + 7) / 8;
   const int max_tiles = cache_tiles + a.n_qtiles;  // the last row block's list
@@ -837,10 +861,10 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     double best = 0.0;
     for (int sp = 1; sp <= kMaxSplitP; ++sp) {
       if (sp > 1 && max_tiles / sp < 8) break;  // keep at least 8 tiles per split
-      const double waves = std::ceil((double)heavy * sp / sms);
+      const double waves = std::ceil((double)heavy_live * sp / sms);
       // streaming CTAs run after the split CTAs: in the last wave's free slots
       // if they fit, else as extra short waves
-      const double spare = waves * sms - (double)heavy * sp;
+      const double spare = waves * sms - (double)heavy_live * sp;
       const double extra = light > spare ? std::ceil((light - spare) / sms) * light_tiles : 0.0;
       const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 3.0 : 1.0)) + extra;
       if (sp == 1 || cost < best * 0.97) {  // split only for a clear gain
