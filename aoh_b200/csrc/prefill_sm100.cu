@@ -676,19 +676,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
         store_row(o, l > 0.f ? 1.f / l : 0.f);
       }
     } else {
-      // split epilogue: this split's partial (O^T so a warp's stores are
-      // contiguous, then m and l per row), a ticket, and the last split to
-      // arrive combines every partial of the row block
+      // split epilogue: this split's partial (O as float4 at [dim / 4][row], so
+      // a warp's 16-byte accesses cover 512 contiguous bytes; then m and l per
+      // row), a ticket, and the last split to arrive combines every partial
+      // of the row block
       const int gslot = item_idx * a.n_qtiles + qtile;
       float* part = a.ws + ((size_t)(gslot * n_split + split) * 2 + q) * kPartFloats;
       if (have) {
+        float4* part4 = reinterpret_cast<float4*>(part);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
           tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
           tc_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) part[(32 * c + e) * BM + row] = __uint_as_float(ov[e]);
+          for (int e = 0; e < 8; ++e)
+            part4[(8 * c + e) * BM + row] = make_float4(__uint_as_float(ov[4 * e]), __uint_as_float(ov[4 * e + 1]),
+                                                        __uint_as_float(ov[4 * e + 2]), __uint_as_float(ov[4 * e + 3]));
         }
       }
       part[BM * kHeadDim + row] = have ? m_used : -INFINITY;
@@ -715,8 +719,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if (!(ls > 0.f)) continue;  // an empty range: no keys for this row
           const float w = fast_exp2(__ldcg(ps + BM * kHeadDim + row) - M);
           L += w * ls;
+          const float4* ps4 = reinterpret_cast<const float4*>(ps);
 #pragma unroll
-          for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(w, __ldcg(ps + d * BM + row), o[d]);
+          for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
+            const float4 v = __ldcg(ps4 + d4 * BM + row);
+            o[4 * d4] = fmaf(w, v.x, o[4 * d4]);
+            o[4 * d4 + 1] = fmaf(w, v.y, o[4 * d4 + 1]);
+            o[4 * d4 + 2] = fmaf(w, v.z, o[4 * d4 + 2]);
+            o[4 * d4 + 3] = fmaf(w, v.w, o[4 * d4 + 3]);
+          }
         }
         store_row(o, L > 0.f ? 1.f / L : 0.f);
         if (tid == 0) a.counters[gslot] = 0;  // ready for the next launch
