@@ -147,3 +147,36 @@ def test_partition_balances_touched_tokens():
     out = np.zeros(1, dtype=np.int32)
     assert L.aoh_partition(bad.ctypes.data_as(C.POINTER(C.c_uint8)), 1, 1, 1, 10, 1, 1, 2,
                            out.ctypes.data_as(C.POINTER(C.c_int32))) == _lib.INVALID
+
+
+def test_gather_entry_points_validate_arguments():
+    """Output-gather entry points: argument errors are reported before any CUDA call."""
+    L = _lib.lib()
+    cfg, keep = _cfg([[1, 0]])
+    rc, h = _create(cfg)
+    assert rc == 0
+    # waiting needs peers
+    assert L.aoh_gather_wait(h, 0, 5, None) == _lib.INVALID and b"no peers" in L.aoh_last_error()
+    regions = (C.c_void_p * 2)(C.c_void_p(4096), C.c_void_p(8192))
+    flags = (C.c_void_p * 2)(C.c_void_p(4096), C.c_void_p(8192))
+    assert L.aoh_kv_set_peers(h, 9, 0, regions, 1024, flags) == _lib.INVALID       # more than 8 ranks
+    assert L.aoh_kv_set_peers(h, 2, 2, regions, 1024, flags) == _lib.INVALID       # rank outside [0, n)
+    assert L.aoh_kv_set_peers(h, 2, 0, None, 1024, flags) == _lib.INVALID         # no region table
+    assert L.aoh_kv_set_peers(h, 2, 0, regions, 0, flags) == _lib.INVALID          # zero-sized regions
+    bad = (C.c_void_p * 2)(C.c_void_p(4096), None)
+    assert L.aoh_kv_set_peers(h, 2, 0, regions, 1024, bad) == _lib.INVALID         # a null flag array
+    odd = (C.c_void_p * 2)(C.c_void_p(4096), C.c_void_p(8194))
+    assert L.aoh_kv_set_peers(h, 2, 0, regions, 1024, odd) == _lib.INVALID         # misaligned flags
+    assert L.aoh_kv_set_peers(h, 0, 0, None, 0, None) == _lib.OK                   # detach is always fine
+    L.aoh_kv_destroy(h)
+    # f32 caches have no gather
+    cfg, keep = _cfg([[1, 0]], dtype=_lib.F32)
+    rc, h = _create(cfg)
+    assert L.aoh_kv_set_peers(h, 2, 0, regions, 1024, flags) == _lib.UNSUPPORTED
+    L.aoh_kv_destroy(h)
+    ptr = C.c_void_p()
+    handle = (C.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+    assert L.aoh_shared_alloc(0, C.byref(ptr), handle) == _lib.INVALID
+    assert L.aoh_shared_alloc(64, None, handle) == _lib.INVALID
+    assert L.aoh_shared_open(None, C.byref(ptr)) == _lib.INVALID
+    assert L.aoh_shared_free(None) == _lib.OK and L.aoh_shared_close(None) == _lib.OK
