@@ -136,12 +136,19 @@ def decode_layer_bytes(T: int, n_ret_units: int, n_str_units: int, B: int) -> in
 # CPU reference (oracle restatement of the reference's eager decode)
 # ----------------------------------------------------------------------------
 
-def cpu_reference_layer_us(n_calls: int, threads: int | None = None):
+def cpu_reference_layer_us(n_calls: int, budget_s: float = 60.0):
     """Time the eager decode of one layer at 128K on the host cores: the
     reference's AoHKVCache state (full retrieval KV, compressed streaming KV)
     and its per-layer forward (torch.cat + repeat_kv + fp32 scores + softmax +
-    P.V + append), restated in numpy.  Returns (us per layer call, threads)."""
+    P.V + append), restated in numpy, with every host core for its BLAS
+    (torchrun sets OMP_NUM_THREADS=1 otherwise).  Stops after n_calls or once
+    budget_s has passed (at least 2 calls).  Returns (us per layer call,
+    threads, calls timed)."""
+    from threadpoolctl import threadpool_limits
+
     from oracle import aoh_oracle as orc
+    threads = os.cpu_count() or 1
+    limiter = threadpool_limits(limits=threads)
     rng = np.random.Generator(np.random.PCG64(SEED))
     labels = np.ones((1, G))
     labels[0, :N_STREAM] = 0.0
@@ -158,18 +165,22 @@ def cpu_reference_layer_us(n_calls: int, threads: int | None = None):
     v = bf(rng.standard_normal((1, 1, G, D), dtype=np.float32) * 0.5)
     orc.layer_attention(cache, 0, q, k, v)  # warm-up
     t0 = time.perf_counter()
-    for _ in range(n_calls):
+    done = 0
+    while done < max(1, n_calls):
         orc.layer_attention(cache, 0, q, k, v)
-    dt = (time.perf_counter() - t0) / n_calls
-    return dt * 1e6, threads or os.cpu_count()
+        done += 1
+        if done >= 2 and time.perf_counter() - t0 > budget_s:
+            break
+    dt = (time.perf_counter() - t0) / done
+    limiter.restore_original_limits()
+    return dt * 1e6, threads, done
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    n = max(1, args.steps)
-    us, cores = cpu_reference_layer_us(n)
+    us, cores, n = cpu_reference_layer_us(max(1, args.steps), budget_s=90.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
         "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(us * L_LAYERS / 1000, 3),
@@ -179,7 +190,8 @@ def run_reference(args):
                    "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
                          "sample": f"{n} decode calls of one layer at 128K (numpy restatement of the reference's "
-                                   "eager AoHKVCache forward); a step is one layer"},
+                                   f"eager AoHKVCache forward, {cores} BLAS threads; at most 90 s of calls); "
+                                   "a step is one layer"},
         "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -399,9 +411,9 @@ def run_aoh(args):
             extras["labels_exact"] = classifier_check(torch, dev)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_calls > 0:
-        us_cpu, cores = cpu_reference_layer_us(args.cpu_calls)
+        us_cpu, cores, n_cpu = cpu_reference_layer_us(args.cpu_calls, budget_s=30.0)
         cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
-               "sample": f"{args.cpu_calls} decode calls of one layer at 128K context (numpy restatement of the "
+               "sample": f"{n_cpu} decode calls of one layer at 128K context (numpy restatement of the "
                          "reference's eager AoHKVCache forward: cat + repeat_kv + fp32 scores + softmax + P.V + "
                          "append)"}
 
