@@ -540,6 +540,76 @@ def prefill_full(torch, dev, bf16_peak, chunk: int, context: int = 65536, layers
             "seconds": round(sec, 4), "flops": flops, "calls": layers * (context // chunk)}
 
 
+def whole_model(torch, dev, context: int = 131072, decode_steps: int = 20, full_baseline: bool = True):
+    """Whole-model decode ms/token, the reference's Table 11 decode column
+    (eval/efficiency/benchmark_llama31.py: decode steps after a long context,
+    sink 128 / window 256): Llama-3.1-8B architecture with random-init bf16
+    weights (no checkpoint is available), 6 of 8 KV heads streaming per layer
+    (sparsity 0.75, labels seeded uniform), patched with patch_aoh_model; and,
+    on the same GPU, the unpatched model with transformers' own attention over
+    a full KV cache (the "full attention" column).  Both caches are filled with
+    synthetic K/V (0.5 * N(0,1)) of `context` tokens instead of running the
+    prefill (decode time depends on the cache's size, not its values; prefill
+    is measured on its own).  Each decode step (one token, its logits) is timed
+    with CUDA events; the median is reported."""
+    from transformers import DynamicCache, LlamaConfig, LlamaForCausalLM
+
+    from aoh_b200 import synthetic as syn
+    from aoh_b200.hf import patch_aoh_model
+    L, KVH = 32, 8
+    cfg = LlamaConfig(hidden_size=4096, intermediate_size=14336, num_hidden_layers=L, num_attention_heads=32,
+                      num_key_value_heads=KVH, head_dim=128, vocab_size=128256, rope_theta=500000.0,
+                      max_position_embeddings=context + decode_steps + 64)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    gen = torch.Generator(device=dev).manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (1, decode_steps + 2), generator=gen, device=dev)
+
+    def decode(cache):
+        times = []
+        with torch.no_grad():
+            model(input_ids=ids[:, :1], past_key_values=cache, use_cache=True)  # warm-up step
+            for t in range(decode_steps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                model(input_ids=ids[:, 1 + t:2 + t], past_key_values=cache, use_cache=True)
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+        return float(np.median(times))
+
+    res = {"model": "llama31_8b_random_init_bf16", "context": context, "decode_steps": decode_steps,
+           "cache": "synthetic K/V of the context length (no prefill)"}
+    if full_baseline:
+        full = DynamicCache()
+        for l in range(L):
+            k = (torch.randn((1, KVH, context, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+            v = (torch.randn((1, KVH, context, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+            full.update(k, v, l)
+            del k, v
+        ms = decode(full)
+        res["full_attention"] = {"decode_ms_per_token": round(ms, 3),
+                                 "attention": str(model.config._attn_implementation)}
+        del full
+        torch.cuda.empty_cache()
+    labels = syn.labels_uniform(SEED, L, KVH, 6)
+    make_cache, n_ret, n_str = patch_aoh_model(model, labels, SINK, RECENT)
+    cache = make_cache(max_context=context + decode_steps + 8)
+    cache.paged.reserve(context + decode_steps + 8)
+    pv = cache.paged.pool_view()
+    for i in range(0, pv.shape[0], 65536):
+        sl = pv[i:i + 65536]
+        sl.copy_((torch.randn(sl.shape, generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16))
+    cache.kv_seq_len = context
+    ms = decode(cache)
+    res["aoh_sp0.75"] = {"decode_ms_per_token": round(ms, 3), "kv_pool_gb": round(cache.paged.pool.numel() / 1e9, 3)}
+    assert cache.paged.device_status() == 0, "device-side check tripped"
+    if full_baseline:
+        res["decode_speedup_vs_full"] = round(res["full_attention"]["decode_ms_per_token"] / ms, 2)
+    return res
+
+
 def classifier_check(torch, dev):
     """AoH classifier on seeded Qwen2.5-7B-shaped projections (28 layers, 28/4
     heads, hidden 3584, bf16): GPU effective ranks -> labels vs the reference's
@@ -607,6 +677,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-classifier", action="store_true")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
+    ap.add_argument("--whole-model", action="store_true",
+                    help="only the whole-model decode ms/token (random-init Llama-3.1-8B, --context tokens)")
     ap.add_argument("--prefill-full", type=int, default=0, metavar="CHUNK",
                     help="only the full 64K chunked prefill at this chunk size")
     ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
@@ -628,6 +700,12 @@ def main():
         torch.cuda.set_device(0)
         _, bf16_peak, _ = measured_peaks()
         print(json.dumps({"prefill": prefill_sample(torch, torch.device("cuda", 0), bf16_peak)}), flush=True)
+        return 0
+    if args.whole_model:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps({"whole_model": whole_model(torch, torch.device("cuda", 0), context=args.context)}),
+              flush=True)
         return 0
     if args.prefill_full:
         import torch
