@@ -34,6 +34,18 @@
 //     nothing waits on another cluster) combines the unit's partials with the
 //     log-sum-exp rule, again spread over its 8 CTAs.  The finishing CTA then
 //     writes the new token's K/V into its page slot (attend, then append).
+//     The ticket is an acq_rel atomic after a cluster barrier: cumulative over
+//     the cluster's partial stores, no per-thread fences.
+//   output gather (multi-GPU, when peers are attached): the CTA that finishes
+//     a unit stores its rows into every rank's output region (peer pointers)
+//     and, after a barrier, publishes a per-(layer, unit) flag to every rank
+//     with one system-scope fence and relaxed stores (gather.cu waits on them).
+//
+// Launches use programmatic dependent launch: the producer streams pages before
+// griddepcontrol.wait (except the page of position T-1, and nothing at all when
+// the previous kernel in the stream wrote this layer), consumers wait before
+// touching q, outputs or the workspace, and dependents are released only after
+// that wait.  Pages stream with an L2 evict-first policy: each is read once.
 #include <cfloat>
 #include <mutex>
 
