@@ -90,13 +90,13 @@ struct DecodeArgs {
   float scale_log2;  // D^-0.5 * log2(e)
   float* ws;         // per-cluster partials, (kMaxCtas / kCluster) x kPartialFloats
   int* counters;     // kMaxUnits tickets, zero between launches
-  // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
-  // bytes for every rank r (its output region as mapped here), then the flag
-  // (layer, unit) of every rank's flag array is set to T + 1
   // 0: the kernel before this one in the stream wrote this layer's pages
   // (e.g. a prefill chunk's append), so no page is streamed before waiting
   // for it; 1: only the page of position T-1 may still be in flight
   int prefetch;
+  // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
+  // bytes for every rank r (its output region as mapped here), then the flag
+  // (layer, unit) of every rank's flag array is set to T + 1
   int n_ranks;
   long long out_delta[kMaxRanks];
   int32_t* flags[kMaxRanks];
