@@ -66,10 +66,9 @@ int aoh_attn_prefill(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q
   if (!q || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_prefill: null q/out");
   if (q_len == 0) return AOH_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (c->cfg.dtype == AOH_BF16)
-    rc = launch_prefill_bf16(c, layer, past_len, q_len, q, k_new, v_new, out, st);
-  else
-    rc = launch_attn_generic(c, layer, past_len, q_len, q, k_new, v_new, out, st);
+  if (c->cfg.dtype == AOH_BF16)  // the tensor-core kernel appends the rows itself
+    return launch_prefill_bf16(c, layer, past_len, q_len, q, k_new, v_new, out, st);
+  rc = launch_attn_generic(c, layer, past_len, q_len, q, k_new, v_new, out, st);
   if (rc) return rc;
   return launch_append(c, layer, past_len, q_len, k_new, v_new, st);
 }

@@ -68,14 +68,16 @@ struct aoh_kv_cache {
   char* out_regions[aoh::kMaxRanks] = {};
   size_t out_bytes = 0;
   int32_t* flag_arrays[aoh::kMaxRanks] = {};
-  // split-KV prefill scratch owned by the cache (grow-only; freed on destroy):
-  // [counters][partials]; the counters are zero between launches
-  // layer whose pages the last stream-ordered write kernel (append, decode
-  // append) touched; a following prefill of another layer may prefetch its
-  // pages before waiting for that kernel
+  // layer whose pages the last stream-ordered write kernel (prefill or decode
+  // with its append, append) touched; a following kernel on another layer may
+  // prefetch its pages before waiting for that kernel
   int last_write_layer = -1;
+  // prefill scratch owned by the cache (grow-only; freed on destroy):
+  // [prefill_cnt_cap ticket counters, padded to 256 B][split partials]; the
+  // counters are zero between launches
   void* prefill_ws = nullptr;
   size_t prefill_ws_bytes = 0;
+  int32_t prefill_cnt_cap = 0;
   ~aoh_kv_cache() {
     if (prefill_ws) cudaFree(prefill_ws);
   }

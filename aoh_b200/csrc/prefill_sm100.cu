@@ -21,9 +21,18 @@
 // pages and the new rows inside the window.
 //
 // Work split: retrieval CTAs may be cut into key ranges (split-KV) so short
-// chunks fill the GPU; each range writes an fp32 partial and the last to
-// finish combines (ticket).  The 1-D grid lists the split CTAs first and the
-// short streaming CTAs last, so the latter fill the final wave.
+// chunks fill the GPU; each range writes a partial (O / l in bf16, m and l in
+// fp32: the combining CTA reads them at one SM's bandwidth, so their size is
+// its time) and the last to finish combines (ticket).  The 1-D grid lists the
+// split CTAs first and the short streaming CTAs last, so the latter fill the
+// final wave.
+//
+// Append: the kernel also writes this call's k/v rows into the layer's pages,
+// so no second kernel sits between two layers' prefills.  Retrieval rows (and
+// every position >= past_len) are never read by the same call, so warp 11 of
+// the group's two-head CTAs copies them while the main loop runs.  Ring slots
+// are read by the unit's streaming CTAs, so the last of those to finish (a
+// ticket taken once its loads have landed) writes the sink and ring rows.
 //
 // Warps (384 threads; setmaxnreg moves registers from warpgroup 2, 72 per
 // thread, to the softmax warpgroups, 216 per thread):
@@ -34,6 +43,7 @@
 //               programmatic dependent launch the producers may fetch their
 //               first cache tiles before waiting for the previous kernel;
 //               q and this call's new rows only after.
+//   warp 11     copies its share of the retrieval unit's new rows to the pages.
 //   warp 9      allocates all 512 TMEM columns and issues the MMAs (the whole
 //               warp runs the loop, lane 0 issues), per key tile i:
 //               S0 = Q0 K_i^T,  O1 += P1(i-1) V_{i-1},  S1 = Q1 K_i^T,
@@ -64,7 +74,7 @@ namespace {
 constexpr int BM = 128;  // query rows per tile (= CTA row block)
 constexpr int BN = 128;  // keys per tile
 constexpr int kPThreads = 384;
-constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // warp 11 only completes warpgroup 2
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10, kWarpAppend = 11;
 // Registers per thread: the kernel is launched with kRegsLaunch (the most 384
 // threads may hold); warpgroup 2 (loads, MMA issue) then gives registers
 // back and the two softmax warpgroups take them.  The shares must fit the
@@ -85,7 +95,9 @@ __device__ __forceinline__ uint32_t col_s(int q) { return q ? 128u : 0u; }    //
 __device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 256u; }  // O_q
 constexpr int kMaxItemsP = 768;
 constexpr int kMaxSplitP = 32;                        // key-range splits of one retrieval CTA
-constexpr int kPartFloats = BM * kHeadDim + 2 * BM;  // one split's partial of one query tile: O^T, m, l
+// One split's partial of one query tile: O / l as bf16, 8 dims per 16 bytes at
+// [dim / 8][row], then m and l (fp32) per row.
+constexpr int kPartBytes = BM * kHeadDim * 2 + 2 * BM * 4;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillArgs {
@@ -104,8 +116,18 @@ struct PrefillArgs {
   // 1: the kernel before this one in the stream wrote another layer's pages,
   // so the first cache tiles may be fetched before waiting for it
   int prefetch;
-  float* ws;
+  uint8_t* ws;
   int* counters;  // one per (retrieval item, row block), zero between launches
+  // Append: the kernel writes this call's k/v rows to the layer's pages.
+  // Retrieval units: warp 11 of the group's two-head CTAs (of its one-head
+  // CTAs when the group has a single head) copies a share of its row block
+  // while the main loop runs; this call reads no page slot at a position
+  // >= T.  Streaming units: the unit's last streaming CTA to finish (ticket in
+  // ring_counters) writes the sink and ring rows once every streaming CTA of
+  // the unit has read the ring.
+  const __nv_bfloat16* k_new;  // (B, C, G, D)
+  const __nv_bfloat16* v_new;
+  int* ring_counters;  // one per (sequence, KV head), zero between launches
   int n_items;
   // ((b * Hq + h0) << 3) | (row_pair << 2) | ((tiles - 1) << 1) | retrieval;
   // retrieval items first.  tiles = 2: heads h0 and h0+1 of one KV group over
@@ -268,6 +290,56 @@ __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+// Writes chunk rows [r_lo, r_hi) of unit (b, g)'s new K and V into its pages:
+// one row per warp instruction (lanes 0-15 K, 16-31 V, 16 bytes each, into the
+// pre-swizzled page layout), kRows rows in flight per warp; warp w of nw takes
+// rows r_lo + kRows * (w + nw * i).  Positions >= sink of a streaming unit go
+// to their ring slot (the caller passes only rows the ring keeps).
+template <int kRows>
+__device__ __forceinline__ void append_rows(const PrefillArgs& a, int b, int g, bool retr, int r_lo, int r_hi,
+                                            int w, int nw, int lane) {
+  const CacheGeom& G = a.geom;
+  const int uidx = (a.layer * G.B + b) * G.G + g;
+  const int32_t* bt = G.block_table + G.unit_offset[uidx];
+  const int cap = G.unit_offset[uidx + 1] - G.unit_offset[uidx];
+  const int kv = lane >> 4, c8 = lane & 15;
+  const size_t row_stride = (size_t)G.G * kHeadDim;  // elements between consecutive rows
+  const __nv_bfloat16* src = (kv ? a.v_new : a.k_new) + (size_t)b * a.C * row_stride + (size_t)g * kHeadDim;
+  uint8_t* pool = static_cast<uint8_t*>(G.pool);
+  for (int r0 = r_lo + kRows * w; r0 < r_hi; r0 += kRows * nw) {
+    uint4 v[kRows];
+    int pid[kRows], slot[kRows];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int r = r0 + k;
+      pid[k] = -2;  // no row
+      if (r < r_hi) {
+        const int p = a.T + r;
+        int j;
+        if (retr || p < G.sink) {
+          j = p / kPage;
+          slot[k] = p % kPage;
+        } else {
+          const int rr = (p - G.sink) % G.ring_cap;
+          j = G.sink_pages + rr / kPage;
+          slot[k] = rr % kPage;
+        }
+        pid[k] = j < cap ? __ldg(bt + j) : -1;
+        v[k] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)r * row_stride) + c8);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      if (pid[k] == -2) continue;
+      if (pid[k] < 0 || pid[k] >= G.num_pages) {
+        if (lane == 0) atomicOr(G.err, kErrBadPage);
+        continue;
+      }
+      *reinterpret_cast<uint4*>(pool + (size_t)pid[k] * kPageBf16Bytes + bf16_chunk_offset(kv, slot[k], c8)) = v[k];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_pool,
@@ -327,6 +399,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
   // this CTA's key tiles: [t_begin, t_begin + n_tiles) of the item's list
   const int t_begin = (int)((long long)tl.n_tiles * split / n_split);
   const int n_tiles = (int)((long long)tl.n_tiles * (split + 1) / n_split) - t_begin;
+  // This CTA's share of its retrieval unit's append: part ap_part of ap_parts
+  // of each of its first ap_blocks row blocks (tiles).  The group's two-head
+  // CTAs share each row block; a one-head group's CTAs write their own.
+  int ap_parts = 0, ap_part = 0;
+  const int ap_blocks = G.grp >= 2 ? 1 : nq;
+  if (retr) {
+    if (G.grp >= 2) {
+      if (!row_pair && nq == 2) {
+        ap_parts = (G.grp / 2) * n_split;
+        ap_part = ((h0 % G.grp) / 2) * n_split + split;
+      }
+    } else {
+      ap_parts = n_split;
+      ap_part = split;
+    }
+  }
 
   if (warp == kWarpMma) {
     tmem_alloc(&s_tmem, kTmemCols);
@@ -521,6 +609,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mma_commit(&bar_final);  // fires once every MMA issued above has completed (both O tiles final)
     }
     __syncwarp();
+  } else if (warp == kWarpAppend && ap_parts > 0) {
+    // ===================== append: retrieval rows =====================
+    griddep_wait();  // this call's rows may be written by the previous kernel
+    for (int blk = 0; blk < ap_blocks; ++blk) {
+      const int rs = q_row0(blk);
+      const int n = min(BM, a.C - rs);
+      if (n > 0)
+        append_rows<4>(a, b, g, true, rs + n * ap_part / ap_parts, rs + n * (ap_part + 1) / ap_parts, 0, 1, lane);
+    }
   }
   } else {
   setmaxnreg_inc<kRegsSoftmax>();
@@ -664,6 +761,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
         reinterpret_cast<uint4*>(dst)[c] = w;
       }
     };
+    auto store_half = [&](const float* o, int hlf, float inv) {  // dims 64 hlf .. 64 hlf + 63 of the row
+      if (qi >= a.C) return;
+#pragma unroll
+      for (int c = 0; c < kHeadDim / 16; ++c) {
+        uint4 w = make_uint4(pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv), pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                             pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv), pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+        reinterpret_cast<uint4*>(dst)[hlf * (kHeadDim / 16) + c] = w;
+      }
+    };
     const bool have = !s_abort && n_tiles > 0 && mbar_wait(&bar_final, 0, G.err);
     if (have) tc_fence_after();
     if (n_split == 1) {
@@ -676,61 +782,117 @@ __global__ void __launch_bounds__(kPThreads, 1)
         store_row(o, l > 0.f ? 1.f / l : 0.f);
       }
     } else {
-      // split epilogue: this split's partial (O as float4 at [dim / 4][row], so
-      // a warp's 16-byte accesses cover 512 contiguous bytes; then m and l per
-      // row), a ticket, and the last split to arrive combines every partial
-      // of the row block
+      // split epilogue: this split's partial (O / l as bf16, 8 dims per 16-byte
+      // store at [dim / 8][row], so a warp's stores cover 512 contiguous
+      // bytes; then m and l per row), a ticket, and the last split to arrive
+      // combines every partial of the row block
       const int gslot = item_idx * a.n_qtiles + qtile;
-      float* part = a.ws + ((size_t)(gslot * n_split + split) * 2 + q) * kPartFloats;
+      uint8_t* part = a.ws + ((size_t)(gslot * n_split + split) * 2 + q) * kPartBytes;
+      float* pml = reinterpret_cast<float*>(part + BM * kHeadDim * 2);
       if (have) {
-        float4* part4 = reinterpret_cast<float4*>(part);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* part8 = reinterpret_cast<uint4*>(part);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
           tmem_ld32(lane_base + col_o(q) + 32 * c, ov);
           tc_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            part4[(8 * c + e) * BM + row] = make_float4(__uint_as_float(ov[4 * e]), __uint_as_float(ov[4 * e + 1]),
-                                                        __uint_as_float(ov[4 * e + 2]), __uint_as_float(ov[4 * e + 3]));
-        }
-      }
-      part[BM * kHeadDim + row] = have ? m_used : -INFINITY;
-      part[BM * kHeadDim + BM + row] = have ? l : 0.f;
-      __threadfence();
-      named_bar_sync(3, nq * 128);
-      if (tid == 0) s_ticket = atomicAdd(&a.counters[gslot], 1);
-      named_bar_sync(3, nq * 128);
-      if (s_ticket == n_split - 1) {
-        __threadfence();
-        const float* p0 = a.ws + ((size_t)gslot * n_split * 2 + q) * kPartFloats;  // split s at + s * 2 * kPartFloats
-        float M = -INFINITY;
-        for (int sp = 0; sp < n_split; ++sp) {
-          const float* ps = p0 + (size_t)sp * 2 * kPartFloats;
-          if (__ldcg(ps + BM * kHeadDim + BM + row) > 0.f) M = fmaxf(M, __ldcg(ps + BM * kHeadDim + row));
-        }
-        float L = 0.f;
-        float o[kHeadDim];
-#pragma unroll
-        for (int d = 0; d < kHeadDim; ++d) o[d] = 0.f;
-        for (int sp = 0; sp < n_split; ++sp) {
-          const float* ps = p0 + (size_t)sp * 2 * kPartFloats;
-          const float ls = __ldcg(ps + BM * kHeadDim + BM + row);
-          if (!(ls > 0.f)) continue;  // an empty range: no keys for this row
-          const float w = fast_exp2(__ldcg(ps + BM * kHeadDim + row) - M);
-          L += w * ls;
-          const float4* ps4 = reinterpret_cast<const float4*>(ps);
-#pragma unroll
-          for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
-            const float4 v = __ldcg(ps4 + d4 * BM + row);
-            o[4 * d4] = fmaf(w, v.x, o[4 * d4]);
-            o[4 * d4 + 1] = fmaf(w, v.y, o[4 * d4 + 1]);
-            o[4 * d4 + 2] = fmaf(w, v.z, o[4 * d4 + 2]);
-            o[4 * d4 + 3] = fmaf(w, v.w, o[4 * d4 + 3]);
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t* o8 = ov + 8 * e;
+            part8[(4 * c + e) * BM + row] =
+                make_uint4(pack_bf16(__uint_as_float(o8[0]) * inv, __uint_as_float(o8[1]) * inv),
+                           pack_bf16(__uint_as_float(o8[2]) * inv, __uint_as_float(o8[3]) * inv),
+                           pack_bf16(__uint_as_float(o8[4]) * inv, __uint_as_float(o8[5]) * inv),
+                           pack_bf16(__uint_as_float(o8[6]) * inv, __uint_as_float(o8[7]) * inv));
           }
         }
-        store_row(o, L > 0.f ? 1.f / L : 0.f);
+      }
+      pml[row] = have ? m_used : -INFINITY;
+      pml[BM + row] = have ? l : 0.f;
+      // The barrier orders every thread's partial stores before the ticket, an
+      // acq_rel atomic at GPU scope: cumulative over those stores (release),
+      // and, for the last split, over the other splits' partials (acquire).
+      named_bar_sync(3, nq * 128);
+      if (tid == 0) {
+        int t;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(t) : "l"(&a.counters[gslot]) : "memory");
+        s_ticket = t;
+      }
+      named_bar_sync(3, nq * 128);
+      if (s_ticket == n_split - 1) {
+        // One pass over the splits per 64-dim half, four splits per batch of
+        // loads (m, l and 8 uint4 of each, issued together): the running
+        // maximum rescales the sums when it grows, so no load waits on
+        // another split's m.  Split s weighs 2^(m_s - M) l_s.
+        constexpr int kB = 4;
+        const uint8_t* p0 = a.ws + ((size_t)gslot * n_split * 2 + q) * kPartBytes;  // split s at + s * 2 * kPartBytes
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          float acc[kHeadDim / 2];
+#pragma unroll
+          for (int d = 0; d < kHeadDim / 2; ++d) acc[d] = 0.f;
+          float M = -INFINITY, L = 0.f;
+          for (int sp = 0; sp < n_split; sp += kB) {
+            uint4 v[kB][kHeadDim / 16];
+            float ms[kB], ls[kB];
+#pragma unroll
+            for (int k = 0; k < kB; ++k) {
+              ms[k] = -INFINITY;
+              ls[k] = 0.f;
+              if (sp + k < n_split) {
+                const uint8_t* ps = p0 + (size_t)(sp + k) * 2 * kPartBytes;
+                const float* qml = reinterpret_cast<const float*>(ps + BM * kHeadDim * 2);
+                ms[k] = __ldcg(qml + row);
+                ls[k] = __ldcg(qml + BM + row);
+                const uint4* v8 = reinterpret_cast<const uint4*>(ps) + hlf * (kHeadDim / 16) * BM + row;
+#pragma unroll
+                for (int d8 = 0; d8 < kHeadDim / 16; ++d8) v[k][d8] = __ldcg(v8 + d8 * BM);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < kB; ++k) {
+              if (!(ls[k] > 0.f)) continue;  // an empty range (or none): no keys for this row
+              const float Mn = fmaxf(M, ms[k]);
+              const float alpha = fast_exp2(M - Mn);  // 0 while nothing is accumulated (M = -inf)
+              const float w = fast_exp2(ms[k] - Mn) * ls[k];
+              L = fmaf(L, alpha, w);
+#pragma unroll
+              for (int d8 = 0; d8 < kHeadDim / 16; ++d8) {
+                const uint32_t u[4] = {v[k][d8].x, v[k][d8].y, v[k][d8].z, v[k][d8].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  acc[8 * d8 + 2 * j] = fmaf(w, bf16_lo(u[j]), acc[8 * d8 + 2 * j] * alpha);
+                  acc[8 * d8 + 2 * j + 1] = fmaf(w, bf16_hi(u[j]), acc[8 * d8 + 2 * j + 1] * alpha);
+                }
+              }
+              M = Mn;
+            }
+          }
+          store_half(acc, hlf, L > 0.f ? 1.f / L : 0.f);
+        }
         if (tid == 0) a.counters[gslot] = 0;  // ready for the next launch
+      }
+    }
+    if (!retr) {
+      // Streaming unit: this CTA's page reads are done (every tile it loaded
+      // was consumed by an MMA before bar_final), so it takes the unit's
+      // ticket; the last of the unit's CTAs writes the sink and ring rows.
+      named_bar_sync(3, nq * 128);
+      if (tid == 0) {
+        int t;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                     : "=r"(t)
+                     : "l"(&a.ring_counters[b * G.G + g])
+                     : "memory");
+        s_ticket = t;
+      }
+      named_bar_sync(3, nq * 128);
+      if (s_ticket == ((G.grp + 1) / 2) * a.n_qtiles - 1) {
+        const int ra_hi = min(a.C, max(0, G.sink - a.T));                         // rows at sink positions
+        const int rb_lo = G.ring_cap > 0 ? max(ra_hi, a.C - G.ring_cap) : a.C;  // rows the ring keeps
+        append_rows<8>(a, b, g, false, 0, ra_hi, warp, nq * 4, lane);
+        append_rows<8>(a, b, g, false, rb_lo, a.C, warp, nq * 4, lane);
+        if (tid == 0) a.ring_counters[b * G.G + g] = 0;  // ready for the next launch
       }
     }
   }
@@ -887,28 +1049,38 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.n_split = n_split;
   a.n_retr_items = n_retr_items;
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
-  a.ws = nullptr;
-  a.counters = nullptr;
-  if (n_split > 1) {
-    const size_t cnt_bytes = ((size_t)heavy * sizeof(int) + 255) / 256 * 256;
-    const size_t need = cnt_bytes + (size_t)heavy * n_split * 2 * kPartFloats * sizeof(float);
-    if (c->prefill_ws_bytes < need) {
-      if (c->prefill_ws) {
-        int rc = cuda_check(cudaStreamSynchronize(st), "prefill: scratch resize");
-        if (rc) return rc;
-        cudaFree(c->prefill_ws);
-        c->prefill_ws = nullptr;
-        c->prefill_ws_bytes = 0;
-      }
-      int rc = cuda_check(cudaMalloc(&c->prefill_ws, need), "prefill: split-KV scratch");
+  c->last_write_layer = layer;  // the kernel appends this call's rows to the layer's pages
+  // Scratch: ticket counters -- one per (sequence, KV head) for the streaming
+  // units' ring append, then one per retrieval slot when split -- in a region
+  // of fixed capacity, so counters never land on an earlier call's partials;
+  // then the split partials.  Growing either part reallocates and zeroes it.
+  const int n_ring = cf.batch * cf.num_kv_heads;
+  const int need_cnt = n_ring + (n_split > 1 ? heavy : 0);
+  const int cnt_cap = std::max(need_cnt, c->prefill_cnt_cap);
+  const size_t cnt_bytes = ((size_t)cnt_cap * sizeof(int) + 255) / 256 * 256;
+  const size_t need = cnt_bytes + (n_split > 1 ? (size_t)heavy * n_split * 2 * kPartBytes : 0);
+  if (c->prefill_ws_bytes < need || c->prefill_cnt_cap < need_cnt) {
+    const size_t bytes = std::max(need, c->prefill_ws_bytes);
+    if (c->prefill_ws) {
+      int rc = cuda_check(cudaStreamSynchronize(st), "prefill: scratch resize");
       if (rc) return rc;
-      c->prefill_ws_bytes = need;
-      rc = cuda_check(cudaMemsetAsync(c->prefill_ws, 0, need, st), "prefill: scratch zero fill");
-      if (rc) return rc;
+      cudaFree(c->prefill_ws);
+      c->prefill_ws = nullptr;
+      c->prefill_ws_bytes = 0;
+      c->prefill_cnt_cap = 0;
     }
-    a.counters = static_cast<int*>(c->prefill_ws);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(c->prefill_ws) + cnt_bytes);
+    int rc = cuda_check(cudaMalloc(&c->prefill_ws, bytes), "prefill: scratch");
+    if (rc) return rc;
+    c->prefill_ws_bytes = bytes;
+    c->prefill_cnt_cap = cnt_cap;
+    rc = cuda_check(cudaMemsetAsync(c->prefill_ws, 0, bytes, st), "prefill: scratch zero fill");
+    if (rc) return rc;
   }
+  a.ring_counters = static_cast<int*>(c->prefill_ws);
+  a.counters = a.ring_counters + n_ring;
+  a.ws = n_split > 1 ? static_cast<uint8_t*>(c->prefill_ws) + cnt_bytes : nullptr;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
   CUtensorMap tq, tk, tv;
   int rc = encode_rows_map(&tq, q, cf.batch, q_len, cf.num_q_heads);
   if (!rc) rc = encode_rows_map(&tk, k_new, cf.batch, q_len, cf.num_kv_heads);

@@ -190,12 +190,14 @@ AOH_API int aoh_attn_decode_noalloc(aoh_kv_cache* cache, int32_t layer, int32_t 
                                     const void* k_new, const void* v_new, void* out, aoh_stream stream);
 
 /* Prefill chunk (any q_len >= 1): causal attention for retrieval heads,
- * sink + window for streaming heads, then append.  bf16 caches: when a chunk
- * has too few row blocks to fill the GPU, retrieval heads are split over key
- * ranges whose partials are combined on the GPU; their scratch belongs to the
- * cache, is allocated on first need and grows (a growing call synchronises
- * `stream` and must not be inside a stream capture), and is freed by
- * aoh_kv_destroy. */
+ * sink + window for streaming heads, then append.  bf16 caches: one kernel
+ * attends and appends; when a chunk has too few row blocks to fill the GPU,
+ * retrieval heads are split over key ranges whose partials (each range's
+ * normalised output in bf16, its max and sum in fp32) are combined on the
+ * GPU.  The kernel's scratch (ticket counters, partials) belongs to the
+ * cache, is allocated by the first call and grows (a growing call
+ * synchronises `stream` and must not be inside a stream capture), and is
+ * freed by aoh_kv_destroy. */
 AOH_API int aoh_attn_prefill(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,
                      const void* q, const void* k_new, const void* v_new, void* out,
                      aoh_stream stream);

@@ -192,6 +192,39 @@ def test_append_layout_roundtrip(cuda_device, dtype):
     assert cache.device_status() == 0
 
 
+@pytest.mark.parametrize("Hq,labels_row", [(4, [1, 0]), (14, [0, 1]), (2, [1, 0])])
+def test_prefill_append_layout(cuda_device, Hq, labels_row):
+    """The bf16 prefill kernel appends its chunk's rows itself (retrieval rows
+    from the two-head CTAs' spare warp, or the one-head CTAs' when the group has
+    one head; streaming sink and ring rows from the unit's last CTA).  After
+    every chunk -- starts off the page grid, across the sink boundary, past ring
+    wraps, a split-KV chunk over a long cache -- every held row equals its
+    input bit for bit, for group sizes 2, 7 and 1."""
+    labels = np.array([labels_row], dtype=np.float64)
+    sink, recent = 20, 40
+    chunks = [100, 37, 200, 300, 1500, 256, 129]
+    T = sum(chunks)
+    cache = AoHKVCache(labels, Hq, batch=2, sink_size=sink, recent_size=recent, max_context=T, dtype=torch.bfloat16)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn((2, T, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    ring = (recent + 15) // 16 * 16
+    s = 0
+    for c in chunks:
+        aoh_attention(cache, 0, q[:, s:s + c].contiguous(), k[:, s:s + c].contiguous(), v[:, s:s + c].contiguous())
+        s += c
+        for seq in range(2):
+            for g in range(2):
+                if labels_row[g]:
+                    pos = list(range(s))
+                else:
+                    pos = list(range(min(sink, s))) + list(range(max(sink, s - ring), s))
+                kk, vv = cache.read_rows(0, seq, g, pos)
+                assert torch.equal(kk, k[seq, pos, g]) and torch.equal(vv, v[seq, pos, g]), (c, seq, g)
+    assert cache.device_status() == 0
+
+
 def test_graph_decode_matches_eager_and_oracle(cuda_device):
     """Decode steps replayed from a CUDA graph (device-resident length,
     programmatic dependent launch between layers) equal the eager path and the
