@@ -1,7 +1,9 @@
 // SIMT attention over (paged cache + this call's keys) for any q_len, and the
 // page-append kernel.  This is the float32 path (head-mixed attention with
 // float32 q/k/v, where the 1e-4 tolerance rules out bf16 tensor-core inputs);
-// bf16 decode uses decode_sm100.cu and bf16 prefill uses prefill_sm100.cu.
+// bf16 decode uses decode_sm100.cu and bf16 prefill uses prefill_sm100.cu, and
+// both of those append their own rows.  The append kernel serves the float32
+// path and aoh_kv_append (either dtype).
 //
 // Reference semantics (eval/efficiency/benchmark_llama31.py:123-132,
 // attention_utils.py:92-119): key p is allowed for the query at position qp iff
@@ -238,11 +240,11 @@ struct AppendArgs {
 };
 
 // One warp per (token, unit): writes the K and V rows of position T + i.
-// Launched with programmatic dependent launch after the attention kernel of
-// the same call: it waits for that kernel (whose CTAs still read the ring
-// slots this overwrites) before writing, and only then lets the next kernel
-// in the stream start, so a starting kernel never overlaps anything older
-// than its immediate predecessor.
+// Launched with programmatic dependent launch (on the float32 path, after the
+// attention kernel of the same call): it waits for the previous kernel (whose
+// CTAs may still read the ring slots this overwrites) before writing, and only
+// then lets the next kernel in the stream start, so a starting kernel never
+// overlaps anything older than its immediate predecessor.
 template <typename T>
 __global__ void __launch_bounds__(128) append_kernel(const AppendArgs a) {
   griddep_wait();
