@@ -263,3 +263,37 @@ def test_graph_decode_matches_eager_and_oracle(cuda_device):
         assert np.abs(f(got[0]) - ref).max() <= 2e-2
     assert graphed.kv_seq_len == eager.kv_seq_len == T + steps
     assert graphed.device_status() == 0 and eager.device_status() == 0
+
+
+def test_prefill_partitioned_cache(cuda_device):
+    """A cache holding only some units (as one rank's share of the multi-GPU
+    partition): the prefill appends exactly the owned units' rows, touches no
+    other unit (such a write would trip the device check word), and the owned
+    heads' outputs match a cache that holds every unit."""
+    labels = np.array([[1, 0]], dtype=np.float64)
+    Hq, grp, sink, recent = 14, 7, 20, 40
+    owned = np.array([[[1, 0], [0, 1]]], dtype=np.uint8)  # seq 0: retrieval group, seq 1: streaming group
+    chunks = [100, 37, 200, 1500, 256]
+    T = sum(chunks)
+    kw = dict(batch=2, sink_size=sink, recent_size=recent, max_context=T, dtype=torch.bfloat16)
+    part = AoHKVCache(labels, Hq, owned=owned, **kw)
+    full = AoHKVCache(labels, Hq, **kw)
+    gen = torch.Generator(device="cuda").manual_seed(10)
+    q = torch.randn((2, T, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn((2, T, 2, 128), generator=gen, device="cuda").to(torch.bfloat16)
+    ring = (recent + 15) // 16 * 16
+    s = 0
+    for c in chunks:
+        args = [x[:, s:s + c].contiguous() for x in (q, k, v)]
+        got = aoh_attention(part, 0, *args)
+        want = aoh_attention(full, 0, *args)
+        s += c
+        for seq, g in ((0, 0), (1, 1)):
+            heads = slice(g * grp, (g + 1) * grp)
+            err = (got[seq, :, heads].float() - want[seq, :, heads].float()).abs().max().item()
+            assert err <= 2e-2, (c, seq, g, err)
+            pos = list(range(s)) if labels[0, g] else list(range(min(sink, s))) + list(range(max(sink, s - ring), s))
+            kk, vv = part.read_rows(0, seq, g, pos)
+            assert torch.equal(kk, k[seq, pos, g]) and torch.equal(vv, v[seq, pos, g]), (c, seq, g)
+    assert part.device_status() == 0 and full.device_status() == 0
