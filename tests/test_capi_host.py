@@ -180,3 +180,26 @@ def test_gather_entry_points_validate_arguments():
     assert L.aoh_shared_alloc(64, None, handle) == _lib.INVALID
     assert L.aoh_shared_open(None, C.byref(ptr)) == _lib.INVALID
     assert L.aoh_shared_free(None) == _lib.OK and L.aoh_shared_close(None) == _lib.OK
+
+
+def test_attention_entry_points_need_a_bound_cache():
+    """The attention entry points report a null cache, or one never bound to
+    device memory, before any CUDA call; the allocation-free decode takes bf16
+    caches only."""
+    L = _lib.lib()
+    buf = C.c_void_p(4096)
+    assert L.aoh_attn_prefill(None, 0, 0, 4, buf, buf, buf, buf, None) == _lib.INVALID
+    assert b"null cache" in L.aoh_last_error()
+    cfg, keep = _cfg([[1, 0]])
+    rc, h = _create(cfg)
+    assert rc == 0
+    assert L.aoh_attn_prefill(h, 0, 0, 4, buf, buf, buf, buf, None) == _lib.STATE
+    assert b"not bound" in L.aoh_last_error()
+    assert L.aoh_attn_decode(h, 0, 0, buf, buf, buf, buf, None, 0, None) == _lib.STATE
+    assert L.aoh_attn_decode_noalloc(h, 0, 0, buf, buf, buf, buf, None) == _lib.STATE
+    assert L.aoh_kv_append(h, 0, 0, 4, buf, buf, None) == _lib.STATE
+    L.aoh_kv_destroy(h)
+    cfg, keep = _cfg([[1, 0]], dtype=_lib.F32)
+    rc, h = _create(cfg)
+    assert L.aoh_attn_decode_noalloc(h, 0, 0, buf, buf, buf, buf, None) == _lib.UNSUPPORTED
+    L.aoh_kv_destroy(h)
