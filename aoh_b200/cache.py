@@ -183,8 +183,14 @@ class AoHKVCache:
         return self.pool.view(self.dtype).view(self.num_pages, 2, PAGE_SIZE, self.head_dim)
 
     def device_status(self) -> int:
+        """Read and clear the device check word (0: no bounds check or bounded
+        wait tripped).  After a timed-out wait the library re-zeroes the ticket
+        counters it owns; the decode workspace is this object's, so it is
+        re-zeroed here."""
         f = C.c_int32()
         _lib.check(self._L.aoh_kv_device_status(self._h, C.byref(f), C.c_void_p(_lib.stream_handle())))
+        if f.value & 2 and self._ws is not None:
+            self._ws.zero_()
         return int(f.value)
 
     def decode_workspace(self) -> torch.Tensor:

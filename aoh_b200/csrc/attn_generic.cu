@@ -332,18 +332,17 @@ int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.qt = std::max(1, kMaxRows / grp);
   a.scale = (float)(1.0 / sqrt((double)kHeadDim));
   dim3 grid((q_len + a.qt - 1) / a.qt, a.n_units);
-  static bool attr_set = false;
-  if (!attr_set) {
-    rc = cuda_check(cudaFuncSetAttribute(attn_generic_kernel<float>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kGenericSmem),
-                    "generic: smem attribute");
-    if (rc) return rc;
-    rc = cuda_check(cudaFuncSetAttribute(attn_generic_kernel<__nv_bfloat16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kGenericSmem),
-                    "generic: smem attribute");
-    if (rc) return rc;
-    attr_set = true;
-  }
+  static PerDeviceOnce attrs;
+  rc = attrs.run(c->device, [] {
+    int r = cuda_check(cudaFuncSetAttribute(attn_generic_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kGenericSmem),
+                       "generic: smem attribute");
+    if (r) return r;
+    return cuda_check(cudaFuncSetAttribute(attn_generic_kernel<__nv_bfloat16>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kGenericSmem),
+                      "generic: smem attribute");
+  });
+  if (rc) return rc;
   if (c->cfg.dtype == AOH_F32)
     attn_generic_kernel<float><<<grid, kGThreads, kGenericSmem, st>>>(a);
   else

@@ -395,18 +395,20 @@ int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_
   double* gram = static_cast<double*>(workspace);
   double* mbuf = gram + (size_t)L * (Hq + G) * kMat;
   double* sbuf = mbuf + (size_t)L * Hq * kMat;
-  static bool attrs = false;
-  if (!attrs) {
-    int rc = cuda_check(cudaFuncSetAttribute(cholesky_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kMat * (int)sizeof(double)),
-                        "cholesky smem attribute");
-    if (rc) return rc;
-    rc = cuda_check(cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kD * kJPitch * (int)sizeof(double)),
-                    "jacobi smem attribute");
-    if (rc) return rc;
-    attrs = true;
-  }
+  static PerDeviceOnce attrs;
+  int device = -1;
+  int rc = current_device(&device);
+  if (rc) return rc;
+  rc = attrs.run(device, [] {
+    int r = cuda_check(cudaFuncSetAttribute(cholesky_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kMat * (int)sizeof(double)),
+                       "cholesky smem attribute");
+    if (r) return r;
+    return cuda_check(cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kD * kJPitch * (int)sizeof(double)),
+                      "jacobi smem attribute");
+  });
+  if (rc) return rc;
   if (dtype == AOH_BF16)
     gram_kernel<__nv_bfloat16><<<dim3(3, L * (Hq + G)), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(wq), static_cast<const __nv_bfloat16*>(wk), Hq, G, d_model, binary, gram);

@@ -8,19 +8,39 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "internal.h"
+
 namespace aoh {
 
-// Device check word bits (written with atomicOr, read by aoh_kv_device_status).
-enum : int {
-  kErrBadPage = 1,        // block-table entry outside the pool
-  kErrWaitTimeout = 2,    // a bounded mbarrier / flag wait gave up
-  kErrBadUnit = 4,        // unit offset outside the table
-};
+// Every wait in this library is bounded in wall-clock time (%globaltimer,
+// nanoseconds), counted from the wait's first unsuccessful poll.  A thread
+// enters an mbarrier wait only after its own griddepcontrol.wait, so the bound
+// covers work of its own grid, never the remaining run time of a predecessor
+// kernel; the gather wait starts early, but its predecessor (a decode kernel)
+// released it only after passing its own griddepcontrol.wait.
+//   kWaitNs: mbarrier phases of this CTA (pages, tiles, MMAs in flight): in
+//     normal operation microseconds.
+//   kPeerWaitNs: flags stored by kernels of other processes (output gather);
+//     covers host-side launch jitter between ranks.
+// Once one wait gives up it sets kErrWaitTimeout in the check word; every
+// other bounded wait that has to poll reads that word and gives up at once, so
+// a stalled grid drains in about one limit instead of one per wait.  The word
+// keeps the bit until aoh_kv_device_status reads and clears it, so launches in
+// between give up at their first slow wait too (their results are void).
+constexpr uint64_t kWaitNs = 250ull * 1000 * 1000;       // 250 ms
+constexpr uint64_t kPeerWaitNs = 1000ull * 1000 * 1000;  // 1 s
 
-// Iteration limit of every spin wait (each try_wait already suspends for a
-// hardware-defined time slice, so this bounds a wait to well under a second
-// of wall time on a healthy GPU while never tripping in normal operation).
-constexpr uint32_t kWaitLimit = 1u << 22;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// True once a bounded wait has given up (this grid, or an earlier launch whose
+// trip has not been read yet).
+__device__ __forceinline__ bool wait_tripped(const int* err) {
+  return err != nullptr && (*reinterpret_cast<const volatile int*>(err) & kErrWaitTimeout) != 0;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -67,14 +87,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records kErrWaitTimeout) if the phase never
-// completed within kWaitLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait: polls in batches, between batches gives up when the
+// check word already says a wait timed out, or records kErrWaitTimeout itself
+// once kWaitNs have passed.
+__device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (wait_tripped(err)) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
   }
-  if (err) atomicOr(err, kErrWaitTimeout);
-  return false;
+}
+
+// Bounded wait: returns false if the phase did not complete within kWaitNs
+// (recording kErrWaitTimeout) or another bounded wait has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err);
 }
 
 // Per-thread register budget of the executing warpgroup (all 128 threads run

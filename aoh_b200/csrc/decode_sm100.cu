@@ -102,15 +102,15 @@ struct DecodeArgs {
   int32_t* flags[kMaxRanks];
 };
 
-// Store one output element (and, when gathering, the same element in every
-// rank's output region).
-__device__ __forceinline__ void store_out(const DecodeArgs& a, __nv_bfloat16* p, float v) {
-  const __nv_bfloat16 h = __float2bfloat16(v);
+// Store 8 consecutive output elements (16 bytes; p is 16-byte aligned) and,
+// when gathering, the same 16 bytes in every rank's output region: one
+// vector store per rank over NVLink.
+__device__ __forceinline__ void store_out8(const DecodeArgs& a, __nv_bfloat16* p, uint4 v) {
   if (a.n_ranks == 0) {
-    *p = h;
+    *reinterpret_cast<uint4*>(p) = v;
     return;
   }
-  for (int r = 0; r < a.n_ranks; ++r) *reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(p) + a.out_delta[r]) = h;
+  for (int r = 0; r < a.n_ranks; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p) + a.out_delta[r]) = v;
 }
 
 // The unit's rows are stored everywhere and the caller's barrier ordered every
@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ volatile int s_abort;
   __shared__ float cp_o[kMaxGrp][kHeadDim];  // this CTA's merged partial (read by its cluster)
   __shared__ float cp_m[kMaxGrp], cp_l[kMaxGrp];
+  __shared__ __align__(16) __nv_bfloat16 s_out[kMaxGrp * kHeadDim / kCluster];  // final slice of a split unit
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -276,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int pid = __shfl_sync(0xffffffffu, my, k);
         // This page may still be receiving the previous kernel's append (when it
         // decoded the same layer): wait for that kernel before loading it.
-        if (v0 + base + k == hot_vj) griddep_wait();
+        // The first reuse of a stage waits for consumers that start only after
+        // that kernel: wait for it first, so the bounded wait times this grid.
+        if (v0 + base + k == hot_vj || base + k == kStages) griddep_wait();
         if (lane == 0 && !s_abort) {
           const int i = base + k, st = i % kStages, rnd = i / kStages;
           bool ok = true;
@@ -486,22 +489,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   __nv_bfloat16* out_u = a.out + ((size_t)b * G.Hq + (size_t)g * grp) * kHeadDim;
-  for (int e = tid; e < grp * kHeadDim; e += kThreads) {
-    const int qq = e >> 7, d = e & (kHeadDim - 1);
-    float M = -INFINITY;
+  if (nsplit == 1) {
+    // 8 consecutive outputs per thread, stored with one 16-byte store per rank
+    for (int c = tid; c < grp * (kHeadDim / 8); c += kThreads) {
+      const int qq = c >> 4, d0 = (c & 15) * 8;
+      float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s_m[w][qq]);
-    const float Mu = M == -INFINITY ? 0.f : M;
-    float acc = 0.f, L = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s_m[w][qq]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, L = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float f = fast_exp2(s_m[w][qq] - Mu);
-      acc += so[(w * kMaxGrp + qq) * kOPitch + d] * f;
-      L += s_l[w][qq] * f;
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float f = fast_exp2(s_m[w][qq] - Mu);
+        const float4* src = reinterpret_cast<const float4*>(so + (w * kMaxGrp + qq) * kOPitch + d0);
+        const float4 x0 = src[0], x1 = src[1];
+        acc[0] += x0.x * f; acc[1] += x0.y * f; acc[2] += x0.z * f; acc[3] += x0.w * f;
+        acc[4] += x1.x * f; acc[5] += x1.y * f; acc[6] += x1.z * f; acc[7] += x1.w * f;
+        L += s_l[w][qq] * f;
+      }
+      const uint4 v = make_uint4(pack_bf16(acc[0] / L, acc[1] / L), pack_bf16(acc[2] / L, acc[3] / L),
+                                 pack_bf16(acc[4] / L, acc[5] / L), pack_bf16(acc[6] / L, acc[7] / L));
+      store_out8(a, out_u + qq * kHeadDim + d0, v);
     }
-    if (nsplit == 1) {
-      store_out(a, out_u + e, acc / L);
-    } else {
+  } else {
+    for (int e = tid; e < grp * kHeadDim; e += kThreads) {
+      const int qq = e >> 7, d = e & (kHeadDim - 1);
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s_m[w][qq]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float acc = 0.f, L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float f = fast_exp2(s_m[w][qq] - Mu);
+        acc += so[(w * kMaxGrp + qq) * kOPitch + d] * f;
+        L += s_l[w][qq] * f;
+      }
       cp_o[qq][d] = acc;
       if (d == 0) {
         cp_m[qq] = M;
@@ -618,8 +641,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16; ++j) acc[j & 3] += v[j] * sw[(k + j) * kMaxGrp + qq];
       }
       for (; k < nk; ++k) acc[0] += __ldcg(po + (size_t)k * kPartialFloats) * sw[k * kMaxGrp + qq];
-      store_out(a, out_u + e, (acc[0] + acc[1]) + (acc[2] + acc[3]));
+      s_out[tid] = __float2bfloat16((acc[0] + acc[1]) + (acc[2] + acc[3]));
     }
+    __syncthreads();
+    // the slice (grp * 16 elements, starting at a multiple of 8) leaves as 16-byte stores
+    for (int c = tid; c < (e_hi - e_lo) / 8; c += kThreads)
+      store_out8(a, out_u + e_lo + 8 * c, reinterpret_cast<const uint4*>(s_out)[c]);
     // the ticket is reset before the unit is published: once every unit of the
     // layer is published, the next kernel may reuse the workspace
     if (rank == 0 && tid == 0) a.counters[u] = 0;
@@ -648,7 +675,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-int g_max_ctas = 0;  // CTAs resident at once when launched in clusters of kCluster
+// CTAs resident at once when launched in clusters of kCluster, per device
+// (filled once per device under g_attrs' lock, read-only afterwards)
+int g_max_ctas[kMaxDevices] = {};
+PerDeviceOnce g_attrs;
 
 // attr must have room for 2 attributes: cluster shape and programmatic
 // stream serialization (the kernel may start while the previous kernel in the
@@ -670,21 +700,24 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
   return cfg;
 }
 
-int ensure_kernel_attrs(int device) {
-  static int configured_device = -1;
-  if (configured_device == device && g_max_ctas > 0) return AOH_OK;
-  int rc = cuda_check(cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kDynSmem),
-                      "decode: set smem attribute");
+// Kernel attributes and the resident-CTA count of `device` (the current one).
+int ensure_kernel_attrs(int device, int* max_ctas) {
+  const int rc = g_attrs.run(device, [device] {
+    int r = cuda_check(cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kDynSmem),
+                       "decode: set smem attribute");
+    if (r) return r;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr, false);
+    int clusters = 0;
+    r = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel, &cfg), "decode: cluster occupancy");
+    if (r) return r;
+    if (clusters <= 0) return fail(AOH_ERR_CUDA, "decode kernel clusters cannot be resident");
+    g_max_ctas[device] = std::min(kMaxCtas, clusters * kCluster);
+    return (int)AOH_OK;
+  });
   if (rc) return rc;
-  cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr, false);
-  int clusters = 0;
-  rc = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel, &cfg), "decode: cluster occupancy");
-  if (rc) return rc;
-  if (clusters <= 0) return fail(AOH_ERR_CUDA, "decode kernel clusters cannot be resident");
-  g_max_ctas = std::min(kMaxCtas, clusters * kCluster);
-  configured_device = device;
+  *max_ctas = g_max_ctas[device];
   return AOH_OK;
 }
 
@@ -714,7 +747,8 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   const int grp = cf.num_q_heads / cf.num_kv_heads;
   if (grp > kMaxGrp)
     return fail(AOH_ERR_UNSUPPORTED, "decode: query heads per KV head (%d) above %d", grp, kMaxGrp);
-  int rc = ensure_kernel_attrs(c->device);
+  int max_ctas = 0;
+  int rc = ensure_kernel_attrs(c->device, &max_ctas);
   if (rc) return rc;
 
   // ---- plan: the units of this layer stored here, split so one wave fills the GPU ----
@@ -739,7 +773,7 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
       ++n;
     }
   if (n == 0) return AOH_OK;
-  const int target = std::min(g_max_ctas, max_clusters * kCluster);
+  const int target = std::min(max_ctas, max_clusters * kCluster);
   int64_t per = std::max<int64_t>(4, (total + target - 1) / target);
   int grid = 0;
   for (;;) {
@@ -833,7 +867,6 @@ constexpr size_t kNoAllocScratchBytes =
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
 
@@ -856,6 +889,13 @@ int noalloc_scratch(int device, cudaStream_t st, void** out) {
 }
 }  // namespace
 
+int noalloc_clear_tickets(int device, cudaStream_t st) {
+  if (device < 0 || device >= kMaxDevices) return AOH_OK;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) return AOH_OK;
+  return cuda_check(cudaMemsetAsync(g_noalloc_ptr[device], 0, kCounterBytes, st), "no-alloc decode: clear tickets");
+}
+
 }  // namespace aoh
 
 extern "C" int aoh_attn_decode_noalloc(aoh_kv_cache* c, int32_t layer, int32_t past_len, const void* q,
@@ -863,7 +903,11 @@ extern "C" int aoh_attn_decode_noalloc(aoh_kv_cache* c, int32_t layer, int32_t p
   using namespace aoh;
   if (c && c->cfg.dtype != AOH_BF16)
     return fail(AOH_ERR_UNSUPPORTED, "aoh_attn_decode_noalloc: bf16 caches only");
-  int rc = check_common(c, layer, past_len, 1, q, k_new, v_new, out, "aoh_attn_decode_noalloc");
+  // AOH_PAST_LEN_DEVICE: the kernel reads the device-resident length; the host
+  // copy sizes the launch, as in aoh_attn_decode
+  const bool dev_len = past_len == AOH_PAST_LEN_DEVICE;
+  const int32_t plan_len = dev_len ? (c ? c->len_hint : 0) : past_len;
+  int rc = check_common(c, layer, plan_len, 1, q, k_new, v_new, out, "aoh_attn_decode_noalloc");
   if (rc) return rc;
   if (!q || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_decode_noalloc: null q/out");
   int n_units = 0;
@@ -884,6 +928,9 @@ extern "C" int aoh_attn_decode_noalloc(aoh_kv_cache* c, int32_t layer, int32_t p
   void* scratch = nullptr;
   rc = noalloc_scratch(dev, st, &scratch);
   if (rc) return rc;
-  // plan_and_launch rejects a plan needing more than kNoAllocClusters partials
-  return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, scratch, kNoAllocClusters, st, nullptr);
+  // The plan never needs more than kNoAllocClusters partials: its grid is at
+  // most max(resident CTAs, kMaxUnits rounded to clusters) = 256 CTAs = 32
+  // clusters; plan_and_launch would reject a larger one.
+  return plan_and_launch(c, layer, plan_len, q, k_new, v_new, out, scratch, kNoAllocClusters, st,
+                         dev_len ? c->dev_err + 1 : nullptr);
 }

@@ -29,8 +29,11 @@ __device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
 }
 
 // One thread per unit of the layer: wait until its flag reaches position + 1.
-// Bounded: each poll sleeps ~100 ns, so a missing peer gives up after about
-// half a second and records kErrWaitTimeout instead of hanging the stream.
+// Bounded in time: a thread polls without pausing for its first few
+// microseconds (a unit usually lands within them), then with short sleeps; a
+// flag that has not arrived after kPeerWaitNs -- or once another wait has
+// recorded a timeout in the check word -- makes it record kErrWaitTimeout and
+// stop, so a missing peer ends the step with an error instead of a hang.
 //
 // Launched with programmatic dependent launch: it starts while this rank's
 // decode of the layer is still running and polls every unit's flag, this
@@ -48,15 +51,17 @@ __global__ void gather_wait_kernel(const int32_t* flags, int base, int n_units, 
   const int want = (T_dev ? *T_dev : T) + 1;
   for (int u = threadIdx.x; u < n_units; u += blockDim.x) {
     const int32_t* f = flags + base + u;
-    bool ok = false;
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-      if (ld_acquire_sys(f) >= want) {
-        ok = true;
+    if (ld_acquire_sys(f) >= want) continue;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+      if (ld_acquire_sys(f) >= want) break;
+      const uint64_t dt = globaltimer_ns() - t0;
+      if (dt > kPeerWaitNs || wait_tripped(err)) {
+        atomicOr(err, kErrWaitTimeout);
         break;
       }
-      __nanosleep(100);
+      if (dt > 4000) __nanosleep(64);
     }
-    if (!ok) atomicOr(err, kErrWaitTimeout);
   }
   griddep_wait();
 }
@@ -148,6 +153,9 @@ int aoh_kv_set_peers(aoh_kv_cache* c, int32_t n_ranks, int32_t rank, void* const
       return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_set_peers: rank %d has a null region", r);
     if (reinterpret_cast<uintptr_t>(flag_arrays[r]) % 4)
       return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_set_peers: rank %d's flag array is not 4-byte aligned", r);
+    // the decode kernel stores outputs 16 bytes at a time at the same offset in every region
+    if (reinterpret_cast<uintptr_t>(out_regions[r]) % 16)
+      return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_kv_set_peers: rank %d's output region is not 16-byte aligned", r);
   }
   // load the wait kernel now: its first launch may happen inside a stream capture
   cudaFuncAttributes fa;

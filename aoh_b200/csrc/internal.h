@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -16,12 +17,40 @@ namespace aoh {
 
 constexpr int kHeadDim = 128;
 constexpr int kPage = 16;
-constexpr int kMaxRanks = 8;  // GPUs of one node taking part in an output gather
+constexpr int kMaxRanks = 8;     // GPUs of one node taking part in an output gather
+constexpr int kMaxDevices = 64;  // device ordinals with per-device state
+
+// Device check word bits (written with atomicOr by the kernels, read and
+// cleared by aoh_kv_device_status).
+enum : int {
+  kErrBadPage = 1,      // block-table entry outside the pool
+  kErrWaitTimeout = 2,  // a bounded mbarrier / flag wait gave up
+  kErrBadUnit = 4,      // unit offset outside the table
+};
 
 // Sets the thread's last-error message and returns `code`.
 int fail(int code, const char* fmt, ...);
 // Wraps a CUDA runtime result.
 int cuda_check(cudaError_t e, const char* what);
+
+// One-time set-up per device (kernel attributes and occupancy are per device):
+// run() calls init() the first time it is asked for `device`, under a lock,
+// and remembers success.
+struct PerDeviceOnce {
+  std::mutex mu;
+  bool done[kMaxDevices] = {};
+  template <class F>
+  int run(int device, F&& init) {
+    if (device < 0 || device >= kMaxDevices) return fail(AOH_ERR_UNSUPPORTED, "device ordinal %d", device);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[device]) return AOH_OK;
+    const int rc = init();
+    if (rc == AOH_OK) done[device] = true;
+    return rc;
+  }
+};
+// The calling thread's current device.
+int current_device(int* device);
 
 // Kernel-side view of the cache geometry (passed by value).
 struct CacheGeom {
@@ -99,6 +128,9 @@ int launch_set_length(aoh_kv_cache* c, int value, int add, cudaStream_t st);
 // Gather-wait kernel for `layer` at position past_len (device length if past_len_dev).
 int launch_gather_wait(aoh_kv_cache* c, int layer, int past_len, const int* past_len_dev, cudaStream_t st);
 size_t decode_workspace_bytes(const aoh_kv_cache* c);
+// Zero the tickets of the allocation-free decode scratch on `device` (if that
+// device has used it), stream-ordered; after a timed-out wait.
+int noalloc_clear_tickets(int device, cudaStream_t st);
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
                         const void* v_new, void* out, cudaStream_t st);
 int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q,

@@ -42,6 +42,8 @@ int cuda_check(cudaError_t e, const char* what) {
   return fail(AOH_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+int current_device(int* device) { return cuda_check(cudaGetDevice(device), "cudaGetDevice"); }
+
 }  // namespace aoh
 
 using namespace aoh;
@@ -377,8 +379,18 @@ int aoh_kv_device_status(aoh_kv_cache* c, int32_t* flags, aoh_stream stream) {
   rc = cuda_check(cudaStreamSynchronize(st), "device status sync");
   if (rc) return rc;
   *flags = v;
-  if (v) return cuda_check(cudaMemsetAsync(c->dev_err, 0, 4, st), "clear check word");
-  return AOH_OK;
+  if (!v) return AOH_OK;
+  rc = cuda_check(cudaMemsetAsync(c->dev_err, 0, 4, st), "clear check word");
+  if (rc || !(v & kErrWaitTimeout)) return rc;
+  // A grid that gave up a wait may have left its ticket counters mid-count:
+  // zero the ones the library owns (prefill scratch, allocation-free decode
+  // scratch).  A caller-owned decode workspace must be re-zeroed by its owner.
+  if (c->prefill_ws && c->prefill_cnt_cap > 0) {
+    rc = cuda_check(cudaMemsetAsync(c->prefill_ws, 0, (size_t)c->prefill_cnt_cap * sizeof(int), st),
+                    "clear prefill tickets");
+    if (rc) return rc;
+  }
+  return noalloc_clear_tickets(c->device, st);
 }
 
 int aoh_partition(const uint8_t* labels, int32_t num_layers, int32_t batch, int32_t num_kv_heads,

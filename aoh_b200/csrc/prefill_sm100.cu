@@ -559,6 +559,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     {
       constexpr uint32_t kIdescQK = idesc_bf16(BM, BN, 0, 0);
       constexpr uint32_t kIdescPV = idesc_bf16(BM, 128, 0, 1);
+      griddep_wait();  // Q arrives only after the previous kernel: the bounded waits time this grid
       bool ok = mbar_wait_warp(&bar_q, 0, G.err);
       tc_fence_after();
       auto qk = [&](int q, int i) {
@@ -631,6 +632,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int i0q = q_row0(q);
     const int qi = i0q + row;
     const float sl2 = a.scale_log2;
+    griddep_wait();  // S depends on Q, loaded after the previous kernel: bounded waits time this grid
     float m_used = -INFINITY;
     int n_masked = 0;  // masked tiles seen so far: picks the key-position buffer
     // P = 2^(s*scale - m) as bf16 over the first 64 columns of S (the whole
@@ -973,8 +975,8 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     int rc = encode_pool_runs_map(c);
     if (rc) return rc;
   }
-  static bool attr_done = false;
-  if (!attr_done) {
+  static PerDeviceOnce attrs;
+  int rc0 = attrs.run(c->device, [] {
     int rc = cuda_check(cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kPSmem),
                         "prefill: smem attribute");
@@ -987,8 +989,9 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     if (fa.numRegs < kRegsLaunch)
       return fail(AOH_ERR_CUDA, "prefill kernel built with %d registers per thread, %d needed by its register split",
                   fa.numRegs, kRegsLaunch);
-    attr_done = true;
-  }
+    return (int)AOH_OK;
+  });
+  if (rc0) return rc0;
   PrefillArgs a;
   a.n_items = 0;
   const int grp = cf.num_q_heads / cf.num_kv_heads;

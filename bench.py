@@ -1,38 +1,49 @@
 #!/usr/bin/env python3
-"""Benchmark: head-mixed decode attention, microseconds per layer at 128K context.
+"""Benchmark: head-mixed decode attention, microseconds per (layer, sequence).
 
-Workload (one step = one decode token through every layer's attention):
+Headline workload (one step = one decode token through every layer's attention):
   Llama-3.1-8B attention shapes (32 query heads, 8 KV heads, head_dim 128),
-  32 layers, bf16, batch 1 per GPU, 131072-token paged context (16-token
+  32 layers, bf16, one sequence per GPU, 131072-token paged context (16-token
   pages), 6 of 8 KV heads streaming per layer (labels seeded uniform), sink 128,
   window 256, KV ~ 0.5*N(0,1), q ~ N(0,1).  Synthetic data (no checkpoint or
-  dataset is needed or available); the cache is filled on the device.
+  dataset is needed or available); every (layer, sequence, KV head) unit's
+  pages are filled on the device from a generator seeded by the unit, so any
+  cache holding that unit -- on any rank -- holds the same values.
 
-  --gpus N > 1 (one process per GPU, torchrun): N sequences of 128K, the
-  (sequence, KV head) units of every layer partitioned across ranks by the
+  --gpus N > 1 (one process per GPU, torchrun): N sequences (weak scaling),
+  the (sequence, KV head) units of every layer partitioned across ranks by the
   longest-processing-time rule on touched KV tokens; each rank attends its
   units and its decode kernel stores every finished unit's output into all
   ranks' output buffers over NVLink (CUDA IPC peer pointers) with a flag per
   unit; a wait kernel per layer is the layer boundary, and the whole step is
-  one CUDA graph (weak scaling: per-GPU work is fixed).  ``--gather nccl``
-  instead all-gathers the outputs with NCCL after each layer, eagerly (the
-  library-collective baseline).  ``value`` is microseconds per (layer,
-  sequence) for the whole job.
+  one CUDA graph.  ``--gather nccl`` instead all-gathers the outputs with NCCL
+  after each layer, eagerly (the library-collective baseline).
 
-Also reported on the same line: the decode kernel's HBM roofline fraction,
-an end-to-end number through the public API with host buffers, the CPU
-reference (the oracle's restatement of the reference's eager path) on a
-bounded sample, bf16 prefill TFLOP/s on a bounded sample of the 64K chunked
-prefill, and the classifier's label agreement with the reference.
+Also on the same line, at every N:
+  * ``parity``: one layer decoded eagerly through the partitioned caches and
+    the gather, against a cache on the same GPU that owns every unit of that
+    layer (same per-unit data, same inputs), max over ranks;
+  * ``batched_256k``: the strong-scaling workload -- Qwen3-8B attention shapes,
+    36 layers, 8 sequences of 262144 tokens, 6 of 8 KV heads streaming with
+    retrieval heads skewed into KV groups 0-1 -- with its own timing, roofline
+    and parity;
+and at N = 1 only: the decode kernel's HBM roofline, an end-to-end number
+through the public API with host buffers, the reference's own eager decode
+timed on the host cores (``cpu_baseline``), bf16 prefill TFLOP/s of the 64K
+chunked prefill with the reference's prefill timed on a window of its last
+chunks, the classifier's labels against the reference's with the reference's
+classify timed in the same run, KV memory accounting, and whole-model decode
+ms/token.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl aoh|reference]
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
-import math
 import os
+import re
 import subprocess
 import sys
 import threading
@@ -44,24 +55,97 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-L_LAYERS, HQ, G, D, T_CTX = 32, 32, 8, 128, 131072
-N_STREAM, SINK, RECENT, KV_SCALE, SEED = 6, 128, 256, 0.5, 0
-METRIC = "decode attn us/layer @128K"
-WORKLOAD = "llama31_8b_decode_128k"
-BATCH_FIXED = 0      # > 0: strong scaling with this many sequences (else one per GPU)
-SKEWED_LABELS = False
+D, SINK, RECENT, KV_SCALE, SEED = 128, 128, 256, 0.5, 0
+WORKLOADS = {
+    # headline: one 128K sequence per GPU (weak scaling)
+    "llama31_8b_decode_128k": dict(layers=32, hq=32, g=8, context=131072, n_stream=6, skewed=False, batch=0,
+                                   metric="decode attn us/layer @128K"),
+    # batched long decode across GPUs: 8 sequences in total (strong scaling)
+    "qwen3_8b_decode_256k_b8": dict(layers=36, hq=32, g=8, context=262144, n_stream=6, skewed=True, batch=8,
+                                    metric="decode attn us/(layer*sequence) @256K batch 8"),
+}
+MAIN = "llama31_8b_decode_128k"
+BATCHED = "qwen3_8b_decode_256k_b8"
+# profiled DRAM bytes per decode launch at 128K, valid while the decode sources are unchanged
+TRAFFIC_PROFILE = ROOT / "profiles" / "decode_bf16_128k_dram.md"
+DECODE_SOURCES = ["aoh_b200/csrc/decode_sm100.cu", "aoh_b200/csrc/common.cuh", "aoh_b200/csrc/page_layout.cuh"]
 
 
 # ----------------------------------------------------------------------------
-# helpers
+# workload description (shared by both arms, so their config keys are equal)
 # ----------------------------------------------------------------------------
 
-def measured_peaks():
+def workload(name: str, context: int | None = None, layers: int | None = None) -> dict:
+    w = dict(WORKLOADS[name], name=name)
+    if context and context != w["context"] or layers and layers != w["layers"]:
+        w["context"] = context or w["context"]
+        w["layers"] = layers or w["layers"]
+        w["name"] = f"{name}_ctx{w['context']}_layers{w['layers']}"
+    return w
+
+
+def n_sequences(w: dict, world: int) -> int:
+    return w["batch"] or world
+
+
+def labels_of(w: dict) -> np.ndarray:
+    from aoh_b200 import synthetic as syn
+    f = syn.labels_skewed if w["skewed"] else syn.labels_uniform
+    return f(SEED, w["layers"], w["g"], w["n_stream"])
+
+
+def decode_layer_bytes(T: int, n_ret_units: int, n_str_units: int, B: int, hq: int) -> int:
+    """Algorithmic HBM bytes of one decode launch (one layer): K+V rows read
+    (retrieval: T cached keys; streaming: min(T, sink+recent)), the new K/V row
+    read once and written once per unit, q read, output written, page ids read."""
+    row = 2 * D * 2  # K + V, bf16
+    kv = n_ret_units * T * row + n_str_units * min(T, SINK + RECENT) * row
+    new = (n_ret_units + n_str_units) * row * 2
+    qo = 2 * B * hq * D * 2
+    tables = n_ret_units * (-(-T // 16)) * 4 + n_str_units * ((SINK + RECENT) // 16) * 4
+    return kv + new + qo + tables
+
+
+def line_config(w: dict, world: int) -> dict:
+    B = n_sequences(w, world)
+    n_ret = w["g"] - w["n_stream"]
+    step_gb = w["layers"] * decode_layer_bytes(w["context"], n_ret * B, w["n_stream"] * B, B, w["hq"]) / 1e9
+    return {"workload": w["name"], "layers": w["layers"], "sequences": B, "context": w["context"],
+            "q_heads": w["hq"], "kv_heads": w["g"], "head_dim": D, "page": 16,
+            "streaming_kv_heads": f"{w['n_stream']}/{w['g']}" + (" (skewed to groups 0-1)" if w["skewed"] else ""),
+            "sink": SINK, "window": RECENT, "parallelism": f"units{world}" if world > 1 else "single",
+            "l2": f"no flush: {step_gb:.2f} GB of KV per step (all ranks) >> 126 MB L2"}
+
+
+def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return {"hbm": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]),
+                "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def decode_sources_sha16() -> str:
+    h = hashlib.sha256()
+    for f in DECODE_SOURCES:
+        h.update((ROOT / f).read_bytes())
+    return h.hexdigest()[:16]
+
+
+def profiled_traffic(context: int):
+    """(bytes per launch, note) from the committed ncu capture of the decode
+    kernel at 128K, only while the decode sources still hash to the profiled ones."""
+    if context != 131072 or not TRAFFIC_PROFILE.exists():
+        return None, "no capture for this context"
+    txt = TRAFFIC_PROFILE.read_text()
+    m = re.search(r"dram_bytes_per_launch = (\d+)", txt)
+    s = re.search(r"decode_sources_sha16 = ([0-9a-f]{16})", txt)
+    if not m or not s:
+        return None, "capture summary incomplete"
+    if s.group(1) != decode_sources_sha16():
+        return None, f"capture predates the current decode sources ({s.group(1)})"
+    return int(m.group(1)), f"ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch at 128K ({TRAFFIC_PROFILE.name})"
 
 
 class ClockSampler:
@@ -71,8 +155,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu):
+        self.gpu = gpu
         self.proc = None
         self.lines = []
         self.thread = None
@@ -120,78 +204,128 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def decode_layer_bytes(T: int, n_ret_units: int, n_str_units: int, B: int) -> int:
-    """Algorithmic HBM bytes of one decode launch (one layer): K+V rows read
-    (retrieval: T cached keys; streaming: min(T, sink+recent)), the new K/V row
-    read once and written once per unit, q read, output written, page ids read."""
-    row = 2 * D * 2  # K + V, bf16
-    kv = n_ret_units * T * row + n_str_units * min(T, SINK + RECENT) * row
-    new = (n_ret_units + n_str_units) * row * 2
-    qo = 2 * B * HQ * D * 2
-    tables = n_ret_units * (-(-T // 16)) * 4 + n_str_units * ((SINK + RECENT) // 16) * 4
-    return kv + new + qo + tables
+def clock_sampler(torch, dev):
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", "") or "")
+    return ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or dev.index))
 
 
 # ----------------------------------------------------------------------------
-# CPU reference (oracle restatement of the reference's eager decode)
+# CPU baselines: the reference's own eager code (baseline/_ref), else the port
 # ----------------------------------------------------------------------------
 
-def cpu_reference_layer_us(n_calls: int, budget_s: float = 60.0):
-    """Time the eager decode of one layer at 128K on the host cores: the
-    reference's AoHKVCache state (full retrieval KV, compressed streaming KV)
-    and its per-layer forward (torch.cat + repeat_kv + fp32 scores + softmax +
-    P.V + append), restated in numpy, with every host core for its BLAS
-    (torchrun sets OMP_NUM_THREADS=1 otherwise).  Stops after n_calls or once
-    budget_s has passed (at least 2 calls).  Returns (us per layer call,
-    threads, calls timed)."""
-    from threadpoolctl import threadpool_limits
+def _reference_or_none():
+    try:
+        from oracle import ref_driver
+        return ref_driver, ref_driver.load(), None
+    except Exception as e:  # not installed / does not import: the numpy port stands in
+        return None, None, f"{type(e).__name__}: {e}"
 
-    from oracle import aoh_oracle as orc
-    threads = os.cpu_count() or 1
-    limiter = threadpool_limits(limits=threads)
-    rng = np.random.Generator(np.random.PCG64(SEED))
-    labels = np.ones((1, G))
-    labels[0, :N_STREAM] = 0.0
-    cache = orc.OracleKVCache(1, labels, SINK, RECENT, "bf16")
-    nr, ns = cache.n_ret[0], cache.n_str[0]
-    bf = orc.bf16_round
-    cache.full_k[0] = bf(rng.standard_normal((1, nr, T_CTX, D), dtype=np.float32) * 0.5)
-    cache.full_v[0] = bf(rng.standard_normal((1, nr, T_CTX, D), dtype=np.float32) * 0.5)
-    cache.stream_k[0] = bf(rng.standard_normal((1, ns, SINK + RECENT, D), dtype=np.float32) * 0.5)
-    cache.stream_v[0] = bf(rng.standard_normal((1, ns, SINK + RECENT, D), dtype=np.float32) * 0.5)
-    cache.kv_seq_len = T_CTX
-    q = bf(rng.standard_normal((1, 1, HQ, D), dtype=np.float32))
-    k = bf(rng.standard_normal((1, 1, G, D), dtype=np.float32) * 0.5)
-    v = bf(rng.standard_normal((1, 1, G, D), dtype=np.float32) * 0.5)
-    orc.layer_attention(cache, 0, q, k, v)  # warm-up
-    t0 = time.perf_counter()
-    done = 0
-    while done < max(1, n_calls):
-        orc.layer_attention(cache, 0, q, k, v)
-        done += 1
-        if done >= 2 and time.perf_counter() - t0 > budget_s:
+
+def cpu_decode_layer(w: dict, warmup: int, steps: int, budget_s: float):
+    """One layer's decode step at the workload's context on the host cores:
+    the reference's patched forward over its AoHKVCache (kind "reference"),
+    or the numpy restatement of it (kind "port") when the reference is not
+    installed.  Warm-up calls, then up to ``steps`` timed calls within
+    ``budget_s`` (at least one).  Returns a dict."""
+    rd, ref, why = _reference_or_none()
+    if ref is not None:
+        cores = rd.use_all_cores()
+        call = rd.decode_layer_call(ref, num_q=w["hq"], num_kv=w["g"], n_stream=w["n_stream"],
+                                    context=w["context"], sink=SINK, recent=RECENT, kv_scale=KV_SCALE, seed=SEED)
+        kind, what = "reference", ("the reference's own make_aoh_forward + AoHKVCache (eval/efficiency/"
+                                   "benchmark_llama31.py), eager torch on the CPU")
+    else:
+        from threadpoolctl import threadpool_limits
+        from oracle import aoh_oracle as orc
+        cores = os.cpu_count() or 1
+        threadpool_limits(limits=cores)
+        rng = np.random.Generator(np.random.PCG64(SEED))
+        labels = np.ones((1, w["g"]))
+        labels[0, :w["n_stream"]] = 0.0
+        cache = orc.OracleKVCache(1, labels, SINK, RECENT, "bf16")
+        nr, ns, T, bf = cache.n_ret[0], cache.n_str[0], w["context"], orc.bf16_round
+        cache.full_k[0] = bf(rng.standard_normal((1, nr, T, D), dtype=np.float32) * KV_SCALE)
+        cache.full_v[0] = bf(rng.standard_normal((1, nr, T, D), dtype=np.float32) * KV_SCALE)
+        keep = min(T, SINK + RECENT)
+        cache.stream_k[0] = bf(rng.standard_normal((1, ns, keep, D), dtype=np.float32) * KV_SCALE)
+        cache.stream_v[0] = bf(rng.standard_normal((1, ns, keep, D), dtype=np.float32) * KV_SCALE)
+        cache.kv_seq_len = T
+        q = bf(rng.standard_normal((1, 1, w["hq"], D), dtype=np.float32))
+        kk = bf(rng.standard_normal((1, 1, w["g"], D), dtype=np.float32) * KV_SCALE)
+        vv = bf(rng.standard_normal((1, 1, w["g"], D), dtype=np.float32) * KV_SCALE)
+        call = lambda: orc.layer_attention(cache, 0, q, kk, vv)  # noqa: E731
+        kind, what = "port", f"numpy restatement of the reference's eager AoHKVCache forward (reference unavailable: {why})"
+    t_start = time.perf_counter()
+    for _ in range(max(1, warmup)):
+        call()
+        if time.perf_counter() - t_start > budget_s / 2:
             break
-    dt = (time.perf_counter() - t0) / done
-    limiter.restore_original_limits()
-    return dt * 1e6, threads, done
+    times = []
+    t0 = time.perf_counter()
+    while len(times) < max(1, steps):
+        s = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - s)
+        if time.perf_counter() - t0 > budget_s:
+            break
+    us = float(np.median(times)) * 1e6
+    return {"us": us, "cores": cores, "kind": kind, "calls": len(times), "what": what,
+            "total_s": float(sum(times))}
 
+
+def cpu_prefill_window(chunk: int = 256, n_chunks: int = 3, context: int = 65536, budget_s: float = 60.0):
+    """The reference's own prefill (Qwen2 patched forward, one layer, 2 of 4 KV
+    heads streaming) over the last ``n_chunks`` chunks of a ``context``-token
+    chunked prefill; the first chunk warms up (its large temporaries fault in)
+    and the rest are timed.  Returns (seconds, masked-in flops, chunks timed,
+    cores, kind) or None when the reference is not installed (the port has no
+    prefill path of comparable cost)."""
+    from aoh_b200.metrics import attention_flops
+    rd, ref, why = _reference_or_none()
+    if ref is None:
+        return None, why
+    cores = rd.use_all_cores()
+    past0 = context - n_chunks * chunk
+    calls = rd.prefill_chunk_calls(ref, past=past0, chunk=chunk, n_chunks=n_chunks, sink=SINK, recent=RECENT,
+                                   seed=SEED)
+    calls[0]()
+    secs, flops, done = 0.0, 0, 0
+    t_all = time.perf_counter()
+    for i, call in enumerate(calls[1:], start=1):
+        s = time.perf_counter()
+        call()
+        secs += time.perf_counter() - s
+        past = past0 + i * chunk
+        flops += 7 * 2 * (attention_flops(chunk, past, True, SINK, RECENT) + attention_flops(chunk, past, False, SINK, RECENT))
+        done += 1
+        if time.perf_counter() - t_all > budget_s:
+            break
+    return (secs, flops, done, cores, "reference"), None
+
+
+# ----------------------------------------------------------------------------
+# reference arm
+# ----------------------------------------------------------------------------
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    us, cores, n = cpu_reference_layer_us(max(1, args.steps), budget_s=90.0)
+    w = workload(args.workload, args.context, args.layers)
+    r = cpu_decode_layer(w, warmup=args.warmup, steps=args.steps, budget_s=150.0)
+    us = r["us"]
+    sample = (f"{r['calls']} timed decode steps of one layer of one sequence at {w['context']} tokens ({r['what']}, "
+              f"{r['cores']} threads; median); a step is one layer of one sequence, whose cost does not depend on "
+              f"how many sequences the job holds")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
-        "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(us * L_LAYERS / 1000, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "layers": L_LAYERS, "batch": 1, "context": T_CTX,
-                   "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT},
-        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
-                         "sample": f"{n} decode calls of one layer at 128K (numpy restatement of the reference's "
-                                   f"eager AoHKVCache forward, {cores} BLAS threads; at most 90 s of calls); "
-                                   "a step is one layer"},
+        "impl": "reference", "metric": w["metric"], "value": round(us, 1), "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": r["calls"], "warmup": args.warmup, "ms_per_step": round(us / 1000, 3),
+        "higher_is_better": False, "scaling": "strong" if w["batch"] else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": line_config(w, world),
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": r["cores"], "kind": r["kind"],
+                         "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -199,67 +333,73 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------------------
-# GPU arm
+# GPU arm: one decode workload (fill, parity, graph, timing, e2e)
 # ----------------------------------------------------------------------------
 
-def run_aoh(args):
-    import torch
-    import torch.distributed as dist
+def unit_seed(l: int, b: int, g: int) -> int:
+    return (SEED * 1_000_003 + (l * 4096 + b) * 64 + g) & 0x7FFFFFFFFFFF
 
-    import aoh_b200
-    from aoh_b200 import AoHKVCache, aoh_attention, synthetic as syn
-    from aoh_b200 import _lib
+
+def fill_units(torch, cache, layer_offset: int = 0) -> None:
+    """Fill every page each stored unit owns, in the unit's own page order, from
+    a generator seeded by (layer + layer_offset, sequence, KV head): two caches
+    holding the same unit with the same page count hold the same values."""
+    pv = cache.pool_view()
+    gen = torch.Generator(device=cache.device)
+    for l in range(cache.num_layers):
+        for b in range(cache.batch):
+            for g in range(cache.num_kv_heads):
+                if cache.owned is not None and not cache.owned[l, b, g]:
+                    continue
+                pages = cache.unit_pages(l, b, g)
+                if not pages:
+                    continue
+                gen.manual_seed(unit_seed(l + layer_offset, b, g))
+                vals = torch.randn((len(pages), 2, 16, D), generator=gen, device=cache.device)
+                pv.index_copy_(0, torch.tensor(pages, dtype=torch.long, device=cache.device),
+                               vals.mul_(KV_SCALE).to(torch.bfloat16))
+
+
+def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: dict, e2e_steps: int,
+               gather: str = "peer") -> dict:
     import ctypes as C
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from aoh_b200 import AoHKVCache, _lib, aoh_attention
 
-    B = BATCH_FIXED or world  # default: one sequence per GPU (weak scaling)
-    labels = (syn.labels_skewed if SKEWED_LABELS else syn.labels_uniform)(SEED, L_LAYERS, G, N_STREAM)
-    n_ret_layer = int((labels[0] >= 0.5).sum())
-    # partition (sequence, KV head) units over ranks
-    owner = np.zeros((L_LAYERS, B, G), dtype=np.int32)
+    L, HQ, G, T = w["layers"], w["hq"], w["g"], w["context"]
+    B = n_sequences(w, world)
+    labels = labels_of(w)
+    owner = np.zeros((L, B, G), dtype=np.int32)
     if world > 1:
         lab_u8 = np.ascontiguousarray(labels >= 0.5, dtype=np.uint8)
-        _lib.check(_lib.lib().aoh_partition(lab_u8.ctypes.data_as(C.POINTER(C.c_uint8)), L_LAYERS, B, G,
-                                            T_CTX, SINK, RECENT, world,
-                                            owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
+        _lib.check(_lib.lib().aoh_partition(lab_u8.ctypes.data_as(C.POINTER(C.c_uint8)), L, B, G, T, SINK, RECENT,
+                                            world, owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
     owned = (owner == rank).astype(np.uint8)
-    max_ctx = T_CTX + args.warmup + args.steps + 2 * (args.e2e_steps + 2) + 4096 + 5 * 400
+    clock_steps = 5 * 400  # pages reserved for the clock warm-up below
+    max_ctx = T + args.warmup + args.steps + 2 * (e2e_steps + 2) + 8 + clock_steps + 16
     cache = AoHKVCache(labels, HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
                        dtype=torch.bfloat16, device=dev, owned=owned, reserve_all=True)
-    gen = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
-    pv = cache.pool_view()
-    for i in range(0, pv.shape[0], 65536):  # fill the pool in slabs (no large fp32 temporaries)
-        sl = pv[i:i + 65536]
-        sl.copy_((torch.randn(sl.shape, generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16))
-    cache.kv_seq_len = T_CTX
-    q = torch.randn((L_LAYERS, B, 1, HQ, D), generator=gen, device=dev).to(torch.bfloat16)
-    kn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
-    vn = (torch.randn((L_LAYERS, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+    fill_units(torch, cache)
+    cache.kv_seq_len = T
+    gen = torch.Generator(device=dev).manual_seed(SEED + 1)  # the same inputs on every rank
+    q = torch.randn((L, B, 1, HQ, D), generator=gen, device=dev).to(torch.bfloat16)
+    kn = (torch.randn((L, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
+    vn = (torch.randn((L, B, 1, G, D), generator=gen, device=dev) * KV_SCALE).to(torch.bfloat16)
     peer = None
-    if world > 1 and args.gather == "peer":
+    if world > 1 and gather == "peer":
         from aoh_b200.gather import PeerGather
-        peer = PeerGather(cache, out_shape=(L_LAYERS, B, 1, HQ, D))
+        peer = PeerGather(cache, out_shape=(L, B, 1, HQ, D))
         out = peer.out  # decoded straight into the shared output region
         out.zero_()
     else:
-        out = torch.zeros((L_LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
+        out = torch.zeros((L, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
 
     # NCCL gather plumbing (--gather nccl): pack owned (b, g) head groups, all-gather, unpack
     if world > 1 and peer is None:
         grp = HQ // G
         packs, unpack = [], []
-        max_units = max(int((owner[l] == r).sum()) for l in range(L_LAYERS) for r in range(world))
-        for l in range(L_LAYERS):
+        max_units = max(int((owner[l] == r).sum()) for l in range(L) for r in range(world))
+        for l in range(L):
             mine = np.flatnonzero(owner[l].ravel() == rank)
             idx = np.full(max_units, mine[0] if len(mine) else 0, dtype=np.int64)
             idx[:len(mine)] = mine
@@ -272,28 +412,50 @@ def run_aoh(args):
             unpack.append((torch.tensor(src, device=dev), torch.tensor(allidx, device=dev)))
         gathered = torch.empty((world * max_units, grp * D), dtype=torch.bfloat16, device=dev)
 
-    def layer(l, q_l, k_l, v_l, o_l):
-        aoh_attention(cache, l, q_l, k_l, v_l, out=o_l)
-        if world > 1:
+    def layer(l, q_l, k_l, v_l, o_l, advance=True):
+        aoh_attention(cache, l, q_l, k_l, v_l, out=o_l, advance=advance)
+        if world > 1 and peer is None:
             flat = o_l.view(B * G, -1)
             mine = flat.index_select(0, packs[l])
             dist.all_gather_into_tensor(gathered, mine)
             src, dst = unpack[l]
             flat.index_copy_(0, dst, gathered.index_select(0, src))
+        elif peer is not None:
+            peer.wait(l, past_len=cache.kv_seq_len)
+
+    # ---- parity: one layer decoded eagerly through this rank's cache and the
+    # gather, against a cache on this GPU that owns every unit of the layer ----
+    lp = L // 2
+    layer(lp, q[lp], kn[lp], vn[lp], out[lp], advance=False)
+    ref = AoHKVCache(labels[lp:lp + 1], HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
+                     dtype=torch.bfloat16, device=dev, reserve_all=True)
+    fill_units(torch, ref, layer_offset=lp)
+    ref.kv_seq_len = T
+    want = aoh_attention(ref, 0, q[lp], kn[lp], vn[lp], advance=False)
+    torch.cuda.synchronize()
+    perr = torch.tensor([(out[lp].float() - want.float()).abs().max().item(),
+                         float(ref.device_status() | cache.device_status())], device=dev)
+    del ref, want
+    torch.cuda.empty_cache()
+    if world > 1:
+        dist.all_reduce(perr, op=dist.ReduceOp.MAX)
+    parity = {"layer": lp, "max_abs_err": float(perr[0]), "tol": 2e-2,
+              "ok": bool(perr[0] <= 2e-2 and perr[1] == 0),
+              "against": "a cache on each rank's GPU owning every unit of the layer (same per-unit data and "
+                         "inputs), after the eager decode through this rank's partition and the output gather; "
+                         "max over ranks"}
 
     graph = None
     if world == 1 or peer is not None:
         from aoh_b200.graph import DecodeStepGraph
         graph = DecodeStepGraph(cache, q, kn, vn, out,
-                                max_steps=args.warmup + args.steps + args.e2e_steps + 8 + 5 * 400,
-                                gather=peer)
-    used_graph = graph is not None
+                                max_steps=args.warmup + args.steps + e2e_steps + 8 + clock_steps, gather=peer)
 
     def step():
         if graph is not None:
             graph.replay()
             return
-        for l in range(L_LAYERS):
+        for l in range(L):
             layer(l, q[l], kn[l], vn[l], out[l])
 
     def barrier():
@@ -301,16 +463,14 @@ def run_aoh(args):
             dist.barrier()
 
     # ---------------- device-timed region ----------------
-    props = torch.cuda.get_device_properties(dev)
-    uuid = str(getattr(props, "uuid", "") or "")
-    clocks = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or local))
+    clocks = clock_sampler(torch, dev)
     clocks.start()  # sampling runs through warm-up and the timed steps (the same steady load)
     for _ in range(args.warmup):
         step()
     # more warm-up until nvidia-smi reports under load (2 s at most); ranks are
     # coupled step by step, so all of them decide together and run the same steps
     t_w = time.perf_counter()
-    for _ in range(400):  # pages are reserved for 5 * 400 extra steps
+    for _ in range(clock_steps // 5):
         torch.cuda.synchronize()
         flags = torch.tensor([0 if clocks.lines else 1, 1 if time.perf_counter() - t_w >= 2.0 else 0],
                              device=dev, dtype=torch.int32)
@@ -328,7 +488,7 @@ def run_aoh(args):
     h0 = time.perf_counter()
     for _ in range(args.steps):
         step()
-    host_us = (time.perf_counter() - h0) * 1e6 / (args.steps * L_LAYERS)
+    host_us = (time.perf_counter() - h0) * 1e6 / (args.steps * L)
     ev1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -338,46 +498,31 @@ def run_aoh(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    assert cache.device_status() == 0, "device-side check tripped"
-    us_layer_seq = ms * 1000.0 / (L_LAYERS * B)
+    status = cache.device_status()
+    assert status == 0, f"device-side check tripped ({status})"
 
-    # roofline of the decode kernel (the only kernel in the N=1 step)
-    hbm, bf16_peak, peak_src = measured_peaks()
+    # roofline of this rank's decode kernel (the only kernel in the N=1 step)
     T_mid = T0 + args.steps // 2
-    n_ret_units = int(((labels >= 0.5)[:, None, :].repeat(B, 1) & (owned > 0)).sum()) // L_LAYERS
-    n_str_units = int(owned.sum()) // L_LAYERS - n_ret_units
-    bytes_launch = decode_layer_bytes(T_mid, n_ret_units, n_str_units, B)
-    launch_us = ms * 1000.0 / L_LAYERS
+    n_ret_units = int(((labels >= 0.5)[:, None, :].repeat(B, 1) & (owned > 0)).sum()) // L
+    n_str_units = int(owned.sum()) // L - n_ret_units
+    bytes_launch = decode_layer_bytes(T_mid, n_ret_units, n_str_units, B, HQ)
+    launch_us = ms * 1000.0 / L
     achieved = bytes_launch / (launch_us * 1e-6) / 1e9
-    # DRAM bytes per launch from the committed ncu summary (64K capture scaled to 128K)
-    traffic = None
-    tp = ROOT / "profiles" / "decode_bf16_64k_ncu_full.md"
-    if tp.exists() and T_CTX == 131072:
-        import re
-        m = re.search(r"dram_bytes_per_launch_128k = (\d+)", tp.read_text())
-        traffic = int(m.group(1)) if m else None
 
     # ---------------- end to end through the public API, host buffers ----------------
     e2e = None
-    if args.e2e_steps > 0:
+    if e2e_steps > 0:
         qh = q.cpu().pin_memory()
         kh = kn.cpu().pin_memory()
         vh = vn.cpu().pin_memory()
         oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        if graph is not None:
-            qd, kd, vd = q, kn, vn  # the graph's input buffers
-        else:
-            qd, kd, vd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+        qd, kd, vd = q, kn, vn  # the graph's (or the eager loop's) input buffers
 
         def e2e_step():
             qd.copy_(qh, non_blocking=True)
             kd.copy_(kh, non_blocking=True)
             vd.copy_(vh, non_blocking=True)
-            if graph is not None:
-                graph.replay()
-            else:
-                for l in range(L_LAYERS):
-                    layer(l, qd[l], kd[l], vd[l], out[l])
+            step()
             oh.copy_(out, non_blocking=True)
 
         e2e_step()
@@ -385,78 +530,54 @@ def run_aoh(args):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.e2e_steps):
+        for _ in range(e2e_steps):
             e2e_step()
         e1.record()
         torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1) / args.e2e_steps
+        ems = e0.elapsed_time(e1) / e2e_steps
         if world > 1:
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = float(t.item())
-        e2e = {"value": round(ems * 1000.0 / (L_LAYERS * B), 2), "unit": "us/layer",
+        e2e = {"value": round(ems * 1000.0 / (L * B), 2), "unit": "us/layer",
                "h2d_bytes_per_step": int(q.numel() + kn.numel() + vn.numel()) * 2,
                "d2h_bytes_per_step": int(out.numel()) * 2}
 
-    extras = {}
-    if rank == 0 and world == 1:
-        if not args.no_prefill:
-            extras["prefill"] = {
-                "workload": "qwen25_7b_chunked_prefill_64k (28 layers, 28/4 heads, 2/4 streaming, bf16)",
-                "chunk_4096": prefill_full(torch, dev, bf16_peak, 4096),
-                "chunk_256": prefill_full(torch, dev, bf16_peak, 256),
-                "kernel_sample": prefill_sample(torch, dev, bf16_peak),
-            }
-        if not args.no_classifier:
-            extras["labels_exact"] = classifier_check(torch, dev)
-    cpu = None
-    if rank == 0 and world == 1 and args.cpu_calls > 0:
-        us_cpu, cores, n_cpu = cpu_reference_layer_us(args.cpu_calls, budget_s=30.0)
-        cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
-               "sample": f"{n_cpu} decode calls of one layer at 128K context (numpy restatement of the "
-                         "reference's eager AoHKVCache forward: cat + repeat_kv + fp32 scores + softmax + P.V + "
-                         "append)"}
+    from aoh_b200 import metrics
+    kv_mem = {"pool_gb_granted_this_rank": round(metrics.kv_pool_gb(cache), 3),
+              "analytical_gb_aoh": round(metrics.kv_storage_gb_aoh(
+                  [int((labels[l] >= 0.5).sum()) * B for l in range(L)],
+                  [int((labels[l] < 0.5).sum()) * B for l in range(L)], D, T, SINK, RECENT), 3),
+              "analytical_gb_full": round(metrics.kv_storage_gb_full(L, G * B, D, T), 3),
+              "note": "analytical: the reference's kv_storage_gb_aoh / _full formulas (all sequences, all ranks) "
+                      "at the context length; granted: pages this rank's pool holds (reserved for the whole run)"}
 
-    if world > 1:
-        graph = None
-        if peer is not None:
-            torch.cuda.synchronize()
-            peer.close()
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return 0
-    line = {
-        "metric": METRIC, "value": round(us_layer_seq, 3), "unit": "us/layer", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
-        "scaling": "strong" if BATCH_FIXED else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "layers": L_LAYERS, "sequences": B, "context": T_CTX,
-                   "q_heads": HQ, "kv_heads": G, "head_dim": D, "page": 16,
-                   "streaming_kv_heads": f"{N_STREAM}/{G}", "sink": SINK, "window": RECENT,
-                   "parallelism": f"units{world}" if world > 1 else "single",
-                   "l2": f"no flush: {bytes_launch * L_LAYERS / 1e9:.2f} GB of KV per step >> 126 MB L2"},
-        "tokens_per_s": round(B / (ms / 1000.0), 2),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,
-                     "kernel": "decode_bf16_kernel", "bytes_per_launch": bytes_launch,
-                     "avg_launch_us": round(launch_us, 3)},
-        "e2e": e2e,
-        "cpu_baseline": cpu,
-        "gpu_launches": (L_LAYERS * (2 if peer is not None else 1) + (1 if used_graph else 0)) * args.steps,
-        "launch_mode": "cuda_graph+pdl" if used_graph else "eager+pdl",
-        "gather": None if world == 1 else ("nvlink_peer_stores" if peer is not None else "nccl_all_gather"),
-        "host_enqueue_us_per_layer": round(host_us, 2),
-        "clocks": clk,
-        **extras,
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    graphed = graph is not None
+    # kernels of this library per timed step: a decode kernel per layer (plus a
+    # gather wait per layer when peers are attached) and the length advance
+    per_step = L * (2 if peer is not None else 1) + (1 if graphed else 0)
+    graph = None
+    if peer is not None:
+        torch.cuda.synchronize()
+        peer.close()
+    cache.close()
+    del cache, q, kn, vn, out
+    torch.cuda.empty_cache()
+    return {"ms": ms, "us_layer_seq": ms * 1000.0 / (L * B), "B": B, "launch_us": launch_us,
+            "bytes_launch": bytes_launch, "achieved": achieved, "e2e": e2e, "parity": parity, "clocks": clk,
+            "host_us": host_us, "gpu_launches": per_step * args.steps, "kv_memory": kv_mem,
+            "launch_mode": "cuda_graph+pdl" if graphed else "eager+pdl",
+            "gather": None if world == 1 else ("nvlink_peer_stores" if peer is not None else "nccl_all_gather")}
 
 
-def prefill_sample(torch, dev, bf16_peak):
+# ----------------------------------------------------------------------------
+# N = 1 extras: prefill, classifier, whole model
+# ----------------------------------------------------------------------------
+
+def prefill_sample(torch, dev, peaks):
     """bf16 prefill TFLOP/s on a bounded sample of the 64K chunked prefill
     (Qwen2.5-7B shapes, one layer, 2 of 4 KV heads streaming): the last 4096-token
-    chunk at 61440 cached tokens."""
+    chunk at 61440 cached tokens.  Three launches of about 2 ms: the burst peak."""
     from aoh_b200 import AoHKVCache, aoh_attention
     from aoh_b200.metrics import attention_flops
     Hq, Gq, past, C = 28, 4, 61440, 4096
@@ -485,26 +606,28 @@ def prefill_sample(torch, dev, bf16_peak):
     grp = Hq // Gq
     flops = 2 * grp * (attention_flops(C, past, True, 128, 256) + attention_flops(C, past, False, 128, 256))
     tf = flops / sec / 1e12
-    return {"tflops": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4), "ms": round(sec * 1e3, 3),
-            "sample": "1 layer, last 4096-token chunk at 61440 cached tokens, Qwen2.5-7B heads, 2/4 streaming",
-            "flops": flops}
+    cache.close()
+    return {"tflops": round(tf, 2), "frac": round(tf / peaks["bf16"], 4), "peak": "bf16 burst (3 launches)",
+            "ms": round(sec * 1e3, 3), "flops": flops,
+            "sample": "1 layer, last 4096-token chunk at 61440 cached tokens, Qwen2.5-7B heads, 2/4 streaming"}
 
 
-def prefill_full(torch, dev, bf16_peak, chunk: int, context: int = 65536, layers: int = 28):
+def prefill_full(torch, dev, peaks, chunk: int, context: int = 65536, layers: int = 28):
     """Chunked prefill to ``context`` tokens through every layer: Qwen2.5-7B
     shapes (28 query / 4 KV heads, head_dim 128), bf16, 2 of 4 KV heads streaming
     per layer (seeded), sink 128, window 256, q/k/v ~ N(0,1) generated once per
     layer and reused for every chunk (values do not change the work).  The whole
     prefill runs twice: the first pass warms up (kernel attributes, split-KV
     scratch sized for every chunk), the second is timed with CUDA events.  Flops
-    count only masked-in (query, key) pairs."""
+    count only masked-in (query, key) pairs; the timed region lasts about half a
+    second, so the fraction is of the sustained bf16 peak."""
     from aoh_b200 import AoHKVCache, aoh_attention
     from aoh_b200 import synthetic as syn
     from aoh_b200.metrics import attention_flops
-    Hq, Gq, sink, recent = 28, 4, 128, 256
+    Hq, Gq = 28, 4
     grp = Hq // Gq
     labels = syn.labels_uniform(31, layers, Gq, 2)
-    cache = AoHKVCache(labels, Hq, batch=1, sink_size=sink, recent_size=recent, max_context=context,
+    cache = AoHKVCache(labels, Hq, batch=1, sink_size=SINK, recent_size=RECENT, max_context=context,
                        dtype=torch.bfloat16, device=dev, reserve_all=True)
     gen = torch.Generator(device=dev).manual_seed(5)
     qs = [torch.randn((1, chunk, Hq, D), generator=gen, device=dev).to(torch.bfloat16) for _ in range(layers)]
@@ -529,15 +652,95 @@ def prefill_full(torch, dev, bf16_peak, chunk: int, context: int = 65536, layers
     sec = e0.elapsed_time(e1) / 1000.0
     flops = 0
     for start in range(0, context, chunk):
-        f_ret = attention_flops(chunk, start, True, sink, recent)
-        f_str = attention_flops(chunk, start, False, sink, recent)
+        f_ret = attention_flops(chunk, start, True, SINK, RECENT)
+        f_str = attention_flops(chunk, start, False, SINK, RECENT)
         for l in range(layers):
             n_ret = int((labels[l] >= 0.5).sum())
             flops += grp * (n_ret * f_ret + (Gq - n_ret) * f_str)
     tf = flops / sec / 1e12
     cache.close()
-    return {"chunk": chunk, "tflops": round(tf, 2), "frac_of_bf16_peak": round(tf / bf16_peak, 4),
-            "seconds": round(sec, 4), "flops": flops, "calls": layers * (context // chunk)}
+    return {"chunk": chunk, "tflops": round(tf, 2), "frac": round(tf / peaks["bf16_sustained"], 4),
+            "peak": "bf16 sustained", "seconds": round(sec, 4), "flops": flops, "calls": layers * (context // chunk)}
+
+
+def prefill_block(torch, dev, peaks):
+    from aoh_b200.metrics import attention_flops
+    res = {"workload": "qwen25_7b_chunked_prefill_64k (28 layers, 28/4 heads, 2/4 streaming, bf16)",
+           "chunk_4096": prefill_full(torch, dev, peaks, 4096),
+           "chunk_256": prefill_full(torch, dev, peaks, 256),
+           "kernel_sample": prefill_sample(torch, dev, peaks)}
+    win, why = cpu_prefill_window()
+    if win is None:
+        res["cpu_baseline"] = {"value": None, "unavailable": why}
+        return res
+    secs, wflops, done, cores, kind = win
+    total = res["chunk_256"]["flops"]
+    extrap = secs * total / wflops
+    res["cpu_baseline"] = {
+        "value": round(extrap, 1), "unit": "s (full 64K prefill at chunk 256, extrapolated)", "cores": cores,
+        "kind": kind, "tflops": round(wflops / secs / 1e12, 4),
+        "sample": (f"{done} 256-token chunks of one layer ending at 65536 tokens (after one untimed chunk), the "
+                   f"reference's own Qwen2 patched forward on the CPU ({cores} threads): {secs:.2f} s for "
+                   f"{wflops:.3e} masked-in flops, scaled to the full prefill's {total:.3e} flops (28 layers, "
+                   f"every chunk) -- the shorter early chunks run at a lower CPU rate, so this favours the CPU"),
+        "vs_gpu_chunk_256": round(extrap / res["chunk_256"]["seconds"], 1)}
+    return res
+
+
+def classifier_block(torch, dev):
+    """AoH classifier on seeded Qwen2.5-7B-shaped projections (28 layers, 28/4
+    heads, hidden 3584, bf16): GPU effective ranks -> labels vs the reference's
+    labels stored in tests/golden/cls_qwen25_7b.npz, both modes, 3 aggregations
+    x 3 sparsities; and the reference's own AoHClassifier.classify on the same
+    weights, timed on the host cores in this run (its labels checked too)."""
+    from aoh_b200 import classifier as clf
+    from aoh_b200 import synthetic as syn
+    z = np.load(ROOT / "tests" / "golden" / "cls_qwen25_7b.npz")
+    L, H, Gk, Dh, dm = 28, 28, 4, 128, 3584
+    bits = [syn.classifier_weights(0, l, H, Gk, Dh, dm) for l in range(L)]
+    wq = torch.empty((L, H * Dh, dm), dtype=torch.bfloat16, device=dev)
+    wk = torch.empty((L, Gk * Dh, dm), dtype=torch.bfloat16, device=dev)
+    for l in range(L):
+        wq[l].copy_(torch.from_numpy(bits[l][0].astype(np.int16)).view(torch.bfloat16))
+        wk[l].copy_(torch.from_numpy(bits[l][1].astype(np.int16)).view(torch.bfloat16))
+    rd, ref, why = _reference_or_none()
+    res = {}
+    for mode in ("fp32", "binary"):
+        clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ranks = clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")
+        sec = time.perf_counter() - t0
+        match = total = sub_noise = 0
+        for agg in ("mean", "min", "max"):
+            kv = clf.aggregate_kv(ranks, Gk, agg)
+            for sp in (0.25, 0.5, 0.75):
+                lab = clf.labels_from_ranks(kv, sp)
+                want = z[f"{mode}_{agg}_sp{sp}_labels"]
+                margins = clf.label_margins(kv, sp)
+                for l in range(L):
+                    total += 1
+                    if np.array_equal(lab[l], want[l]):
+                        match += 1
+                    elif margins[l] < 2e-6:
+                        sub_noise += 1
+        rel = float(np.max(np.abs(ranks - z[f"{mode}_eff_ranks_q"]) / z[f"{mode}_eff_ranks_q"]))
+        r = {"layer_decisions_equal": f"{match}/{total}", "differ_below_ref_fp32_noise": sub_noise,
+             "max_rel_rank_err": rel, "gpu_seconds": round(sec, 4)}
+        if ref is not None:
+            cores = rd.use_all_cores()
+            secs, labels = rd.classify_seconds(ref, [b[0] for b in bits], [b[1] for b in bits], H, Gk, dm,
+                                               binary=mode == "binary", agg="mean", sparsity=0.5)
+            r["cpu_baseline"] = {"value": round(secs, 3), "unit": "s per classify (28 x 28 heads)", "cores": cores,
+                                 "kind": "reference",
+                                 "sample": "the reference's own AoHClassifier.classify (agg mean, sparsity 0.5) "
+                                           "on the same bf16 weights, on the host cores in this run",
+                                 "labels_equal_stored": bool(np.array_equal(labels, z[f"{mode}_mean_sp0.5_labels"]))}
+            r["vs_cpu"] = round(secs / sec, 1)
+        else:
+            r["cpu_baseline"] = {"value": None, "unavailable": why}
+        res[mode] = r
+    return res
 
 
 def whole_model(torch, dev, context: int = 131072, decode_steps: int = 20, full_baseline: bool = True):
@@ -580,7 +783,9 @@ def whole_model(torch, dev, context: int = 131072, decode_steps: int = 20, full_
         return float(np.median(times))
 
     res = {"model": "llama31_8b_random_init_bf16", "context": context, "decode_steps": decode_steps,
-           "cache": "synthetic K/V of the context length (no prefill)"}
+           "cache": "synthetic K/V of the context length (no prefill)",
+           "reference_table11_ms_per_token_128k": {"full": 199.55, "aoh_sp0.75": 49.90,
+                                                   "note": "published, hardware not stated"}}
     if full_baseline:
         full = DynamicCache()
         for l in range(L):
@@ -607,63 +812,95 @@ def whole_model(torch, dev, context: int = 131072, decode_steps: int = 20, full_
     assert cache.paged.device_status() == 0, "device-side check tripped"
     if full_baseline:
         res["decode_speedup_vs_full"] = round(res["full_attention"]["decode_ms_per_token"] / ms, 2)
+    cache.paged.close()
+    del model, cache
+    torch.cuda.empty_cache()
     return res
 
 
-def classifier_check(torch, dev):
-    """AoH classifier on seeded Qwen2.5-7B-shaped projections (28 layers, 28/4
-    heads, hidden 3584, bf16): GPU effective ranks -> labels vs the reference's
-    labels stored in tests/golden/cls_qwen25_7b.npz, both modes, 3 aggregations
-    x 3 sparsities."""
-    from aoh_b200 import classifier as clf
-    from aoh_b200 import synthetic as syn
-    z = np.load(ROOT / "tests" / "golden" / "cls_qwen25_7b.npz")
-    L, H, Gk, Dh, dm = 28, 28, 4, 128, 3584
-    wq = torch.empty((L, H * Dh, dm), dtype=torch.bfloat16, device=dev)
-    wk = torch.empty((L, Gk * Dh, dm), dtype=torch.bfloat16, device=dev)
-    for l in range(L):
-        a, b = syn.classifier_weights(0, l, H, Gk, Dh, dm)
-        wq[l].copy_(torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16))
-        wk[l].copy_(torch.from_numpy(b.astype(np.int16)).view(torch.bfloat16))
-    res = {}
-    for mode in ("fp32", "binary"):
-        clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")  # warm-up
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        ranks = clf.eff_ranks_from_weights(wq, wk, H, Gk, Dh, binary=mode == "binary")
-        sec = time.perf_counter() - t0
-        match = total = sub_noise = 0
-        for agg in ("mean", "min", "max"):
-            kv = clf.aggregate_kv(ranks, Gk, agg)
-            for sp in (0.25, 0.5, 0.75):
-                lab = clf.labels_from_ranks(kv, sp)
-                want = z[f"{mode}_{agg}_sp{sp}_labels"]
-                margins = clf.label_margins(kv, sp)
-                for l in range(L):
-                    total += 1
-                    if np.array_equal(lab[l], want[l]):
-                        match += 1
-                    elif margins[l] < 2e-6:
-                        sub_noise += 1
-        rel = float(np.max(np.abs(ranks - z[f"{mode}_eff_ranks_q"]) / z[f"{mode}_eff_ranks_q"]))
-        res[mode] = {"layer_decisions_equal": f"{match}/{total}", "differ_below_ref_fp32_noise": sub_noise,
-                     "max_rel_rank_err": rel, "gpu_seconds": round(sec, 4),
-                     "ref_cpu_seconds": round(float(z[f"{mode}_classify_seconds"]), 3)}
-    return res
+# ----------------------------------------------------------------------------
+# GPU arm: the line
+# ----------------------------------------------------------------------------
 
+def run_aoh(args):
+    import torch
+    import torch.distributed as dist
 
-def _set_workload(context: int, layers: int, name: str = "llama31_8b_decode_128k") -> None:
-    global T_CTX, L_LAYERS, WORKLOAD, BATCH_FIXED, SKEWED_LABELS, METRIC
-    if name == "qwen3_8b_decode_256k_b8":
-        # batched long decode across GPUs: Qwen3-8B attention shapes (32 query /
-        # 8 KV heads), 36 layers, 8 sequences of 262144 tokens, 6/8 streaming,
-        # retrieval heads clustered in KV groups 0-1; strong scaling
-        T_CTX, L_LAYERS, BATCH_FIXED, SKEWED_LABELS = 262144, 36, 8, True
-        WORKLOAD, METRIC = name, "decode attn us/(layer*sequence) @256K batch 8"
-        return
-    if context != T_CTX or layers != L_LAYERS:
-        T_CTX, L_LAYERS = context, layers
-        WORKLOAD = f"llama31_8b_decode_{T_CTX}_ctx_{L_LAYERS}_layers"
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    import aoh_b200  # noqa: F401  (loads libaoh.so; fails loudly without it)
+
+    peaks = measured_peaks()
+    w = workload(args.workload, args.context, args.layers)
+    main = run_decode(torch, dist, w, args, world, rank, dev, peaks, args.e2e_steps, args.gather)
+    batched = None
+    if not args.no_batched and w["name"] != BATCHED and args.gather == "peer":
+        wb = workload(BATCHED)
+        b = run_decode(torch, dist, wb, args, world, rank, dev, peaks, 0)
+        batched = {"metric": wb["metric"], "value": round(b["us_layer_seq"], 3), "unit": "us/(layer*sequence)",
+                   "ms_per_step": round(b["ms"], 4), "steps": args.steps, "scaling": "strong",
+                   "config": line_config(wb, world),
+                   "roofline_this_rank": {"bound": "hbm", "achieved": round(b["achieved"], 1), "peak": peaks["hbm"],
+                                          "unit": "GB/s", "frac": round(b["achieved"] / peaks["hbm"], 4),
+                                          "bytes_per_launch": b["bytes_launch"],
+                                          "avg_launch_us": round(b["launch_us"], 3)},
+                   "parity": b["parity"], "clocks": b["clocks"], "kv_memory": b["kv_memory"],
+                   "gpu_launches": b["gpu_launches"]}
+
+    extras = {}
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_prefill:
+            extras["prefill"] = prefill_block(torch, dev, peaks)
+        if not args.no_classifier:
+            extras["labels_exact"] = classifier_block(torch, dev)
+        if not args.no_whole_model:
+            extras["whole_model"] = whole_model(torch, dev)
+        if args.cpu_calls > 0:
+            r = cpu_decode_layer(w, warmup=1, steps=args.cpu_calls, budget_s=30.0)
+            cpu = {"value": round(r["us"], 1), "unit": "us/layer", "cores": r["cores"], "kind": r["kind"],
+                   "sample": f"{r['calls']} decode steps of one layer of one sequence at {w['context']} tokens "
+                             f"({r['what']}; median, after one untimed step)"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    traffic, traffic_note = profiled_traffic(w["context"])
+    line = {
+        "metric": w["metric"], "value": round(main["us_layer_seq"], 3), "unit": "us/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 4), "higher_is_better": False,
+        "scaling": "strong" if w["batch"] else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": line_config(w, world),
+        "tokens_per_s": round(main["B"] / (main["ms"] / 1000.0), 2),
+        "roofline": {"bound": "hbm", "achieved": round(main["achieved"], 1), "peak": peaks["hbm"], "unit": "GB/s",
+                     "frac": round(main["achieved"] / peaks["hbm"], 4), "traffic": traffic,
+                     "traffic_source": traffic_note, "peak_source": peaks["source"] + " (copy bandwidth)",
+                     "kernel": "decode_bf16_kernel", "bytes_per_launch": main["bytes_launch"],
+                     "avg_launch_us": round(main["launch_us"], 3)},
+        "e2e": main["e2e"],
+        "cpu_baseline": cpu,
+        "parity": main["parity"],
+        "gpu_launches": main["gpu_launches"],
+        "launch_mode": main["launch_mode"],
+        "gather": main["gather"],
+        "host_enqueue_us_per_layer": round(main["host_us"], 2),
+        "clocks": main["clocks"],
+        "kv_memory": main["kv_memory"],
+        "batched_256k": batched,
+        **extras,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -673,46 +910,40 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["aoh", "reference"], default="aoh")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--cpu-calls", type=int, default=10)
+    ap.add_argument("--cpu-calls", type=int, default=5)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-classifier", action="store_true")
+    ap.add_argument("--no-whole-model", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the 8-sequence 256K strong-scaling workload")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
     ap.add_argument("--whole-model", action="store_true",
                     help="only the whole-model decode ms/token (random-init Llama-3.1-8B, --context tokens)")
     ap.add_argument("--prefill-full", type=int, default=0, metavar="CHUNK",
                     help="only the full 64K chunked prefill at this chunk size")
-    ap.add_argument("--context", type=int, default=131072, help="cached tokens (profiling cases)")
-    ap.add_argument("--layers", type=int, default=32, help="layers (profiling cases)")
-    ap.add_argument("--workload", choices=["llama31_8b_decode_128k", "qwen3_8b_decode_256k_b8"],
-                    default="llama31_8b_decode_128k",
-                    help="decode workload; the second is the 8-sequence 256K strong-scaling case")
+    ap.add_argument("--context", type=int, default=0, help="cached tokens (profiling cases; default: the workload's)")
+    ap.add_argument("--layers", type=int, default=0, help="layers (profiling cases; default: the workload's)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=MAIN,
+                    help="headline decode workload; the 256K batch-8 one also runs after it unless --no-batched")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: output gather by peer stores from the decode kernel, or NCCL all-gather")
     args = ap.parse_args()
-    _set_workload(args.context, args.layers, args.workload)
     if args.warmup < 3 and args.impl == "aoh":
         print("note: --warmup raised to 3", file=sys.stderr)
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.prefill_only:
+    if args.prefill_only or args.whole_model or args.prefill_full:
         import torch
         torch.cuda.set_device(0)
-        _, bf16_peak, _ = measured_peaks()
-        print(json.dumps({"prefill": prefill_sample(torch, torch.device("cuda", 0), bf16_peak)}), flush=True)
-        return 0
-    if args.whole_model:
-        import torch
-        torch.cuda.set_device(0)
-        print(json.dumps({"whole_model": whole_model(torch, torch.device("cuda", 0), context=args.context)}),
-              flush=True)
-        return 0
-    if args.prefill_full:
-        import torch
-        torch.cuda.set_device(0)
-        _, bf16_peak, _ = measured_peaks()
-        print(json.dumps({"prefill": prefill_full(torch, torch.device("cuda", 0), bf16_peak, args.prefill_full)}),
-              flush=True)
+        dev = torch.device("cuda", 0)
+        peaks = measured_peaks()
+        if args.prefill_only:
+            res = {"prefill": prefill_sample(torch, dev, peaks)}
+        elif args.whole_model:
+            res = {"whole_model": whole_model(torch, dev, context=args.context or 131072)}
+        else:
+            res = {"prefill": prefill_full(torch, dev, peaks, args.prefill_full)}
+        print(json.dumps(res), flush=True)
         return 0
     return run_aoh(args)
 

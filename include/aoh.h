@@ -131,7 +131,14 @@ AOH_API int aoh_kv_locate(const aoh_kv_cache* cache, int32_t layer, int32_t seq,
                           int32_t position, int32_t past_len, int32_t* page, int32_t* slot);
 
 /* Read and clear the device-side check word (bounds checks, bounded waits);
- * synchronizes `stream`. *flags == 0 means no check tripped. */
+ * synchronizes `stream`. *flags == 0 means no check tripped.  Bit 1: a
+ * block-table entry outside the pool (the page was skipped); bit 2: a bounded
+ * wait gave up (250 ms for a CTA's own pipeline, 1 s for a peer's gather
+ * flag) -- until this call clears the bit, later launches give up at their
+ * first slow wait too, and their results are void.  On bit 2 this call also
+ * re-zeroes the ticket counters the library owns (prefill scratch, the
+ * allocation-free decode scratch); a caller-owned decode workspace must be
+ * re-zeroed by the caller before its next use. */
 AOH_API int aoh_kv_device_status(aoh_kv_cache* cache, int32_t* flags, aoh_stream stream);
 
 /* ------------------------------------------------------------------------- */
@@ -168,7 +175,8 @@ AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len
                     const void* k_new, const void* v_new, void* out, void* workspace,
                     size_t workspace_bytes, aoh_stream stream);
 
-/* aoh_attn_decode without a workspace argument, for callers that cannot
+/* aoh_attn_decode without a workspace argument (past_len may be
+ * AOH_PAST_LEN_DEVICE, as for aoh_attn_decode), for callers that cannot
  * allocate device memory: plugin hosts that hand an op only its input and
  * output buffers and own every allocation themselves, and runtimes that may
  * not allocate after start-up (fixed memory budgets, allocators that are not

@@ -267,6 +267,67 @@ def decode_from_state(q, k_new, v_new, k_ctx, v_ctx, labels_row, past_len: int,
     return out
 
 
+def attend_rows(q_rows, q_pos, k_hist, v_hist, retrieval: bool, sink_size: int, recent_size: int,
+                dtype: str, block: int = 32) -> np.ndarray:
+    """Chosen query rows of one KV group over its full key history, for checks
+    at full context sizes where running every row is too slow.
+
+    ``q_rows`` (R, grp, D) at positions ``q_pos`` (R,); ``k_hist``/``v_hist``
+    (S, D) hold positions 0..S-1 of the group's keys (cached ones and this
+    chunk's).  A retrieval row at position p sees keys 0..p (the causal mask
+    offset by past_len, benchmark_llama31.py:116-120 and :123-132); a streaming
+    row sees keys k <= p with k < sink or k >= p - recent
+    (attention_utils.py:109-114), which are exactly the keys the reference's
+    compressed cache plus the chunk still hold for it (compress_stream keeps the
+    last ``recent`` cached positions, :23-42).  Same arithmetic as the
+    reference: fp32 scores times D^-0.5, masked scores finfo(float32).min,
+    fp32 softmax, probabilities rounded to the input dtype, fp32 P.V rounded to
+    the input dtype.  GQA expansion (repeat_kv) only copies, so the group's
+    query heads are evaluated against the one KV head directly.
+    -> (R, grp, D) float32."""
+    q_rows = np.asarray(q_rows, dtype=F32)
+    R, grp, D = q_rows.shape
+    scale = F32(D ** -0.5)
+    kf = np.asarray(k_hist, dtype=F32)
+    vf = np.asarray(v_hist, dtype=F32)
+    kpos = np.arange(kf.shape[0])
+    out = np.empty((R, grp, D), dtype=F32)
+    for r0 in range(0, R, block):
+        r1 = min(R, r0 + block)
+        p = np.asarray(q_pos[r0:r1])[:, None]
+        hi = int(p.max()) + 1
+        allowed = kpos[None, :hi] <= p
+        if not retrieval:
+            allowed &= (kpos[None, :hi] < sink_size) | (kpos[None, :hi] >= p - recent_size)
+        scores = np.matmul(q_rows[r0:r1], kf[:hi].T) * scale                 # (r, grp, hi)
+        scores = np.where(allowed[:, None, :], scores, _NEG).astype(F32)
+        out[r0:r1] = _pv(_softmax_f32(scores), vf[:hi], dtype)
+    return out
+
+
+def decode_unit(q_grp, k_new, v_new, k_cached, v_cached, retrieval: bool, past_len: int,
+                sink_size: int, recent_size: int, dtype: str) -> np.ndarray:
+    """Decode step (q_len = 1) of one (sequence, KV head) unit: what
+    :func:`layer_attention` computes for that unit, from the unit's cached rows
+    as AoHKVCache holds them (retrieval: all ``past_len`` rows; streaming:
+    ``compress_stream`` of the history, sink then recent rows).
+    ``q_grp`` (grp, D), ``k_new``/``v_new`` (D,), ``k_cached``/``v_cached``
+    (S, D).  Retrieval: eager_attention without a mask (q_len = 1,
+    benchmark_llama31.py:123-132); streaming: streaming_attention
+    (attention_utils.py:92-119).  GQA expansion (repeat_kv) only copies, so the
+    group's query heads are evaluated against the one KV head directly.
+    -> (grp, D) float32."""
+    q = np.asarray(q_grp, dtype=F32)[None, :, None, :]                        # (1, grp, 1, D)
+    kk = np.concatenate([np.asarray(k_cached, dtype=F32), np.asarray(k_new, dtype=F32)[None]], 0)[None, None]
+    vv = np.concatenate([np.asarray(v_cached, dtype=F32), np.asarray(v_new, dtype=F32)[None]], 0)[None, None]
+    if retrieval:
+        o = eager_attention(q, kk, vv, past_len, False, dtype)
+    else:
+        o = streaming_attention(q, kk, vv, past_len=past_len, cached_len=kk.shape[2] - 1,
+                                sink_size=sink_size, recent_size=recent_size, dtype=dtype)
+    return o[0, :, 0]
+
+
 # ----------------------------------------------------------------------------
 # effective-rank classifier
 # ----------------------------------------------------------------------------

@@ -24,41 +24,17 @@ def test_golden_cases(cuda_device, name):
     assert err <= tol, f"{name}: max abs err {err} > {tol}"
 
 
-def _run_both(dtype, Hq, G, labels, chunks, decode, sink, recent, seed, batch=1, kv_scale=1.0):
-    """Run the same seeded sequence through the oracle and the CUDA path; return
-    the worst error per step kind."""
-    L = labels.shape[0]
-    total = sum(chunks) + decode
-    inputs = [syn.attn_layer_inputs(seed, l, batch, total, Hq, G, 128, dtype=dtype, kv_scale=kv_scale)
-              for l in range(L)]
-    oc = orc.OracleKVCache(L, labels, sink, recent, dtype)
-    gcache = AoHKVCache(labels, Hq, batch=batch, sink_size=sink, recent_size=recent, max_context=total,
-                        dtype=ge.DTYPES[dtype])
-    errs = {"prefill": 0.0, "decode": 0.0}
-    start = 0
-    for c in list(chunks) + [1] * decode:
-        for l in range(L):
-            q, k, v = (x[:, start:start + c] for x in inputs[l])
-            want = orc.layer_attention(oc, l, q, k, v)
-            got = ge.step(gcache, l, q, k, v)
-            kind = "decode" if c == 1 else "prefill"
-            errs[kind] = max(errs[kind], float(np.abs(got - want).max()))
-        start += c
-    assert gcache.device_status() == 0
-    return errs
-
-
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_llama_shapes_against_oracle(cuda_device, dtype):
     labels = syn.labels_uniform(3, 2, 8, 6)
-    errs = _run_both(dtype, 32, 8, labels, [256, 256, 300], 5, 128, 256, seed=21)
+    errs = ge.run_both(dtype, 32, 8, labels, [256, 256, 300], 5, 128, 256, seed=21)
     tol = gc.TOL[dtype]
     assert errs["prefill"] <= tol and errs["decode"] <= tol, errs
 
 
 def test_qwen25_group7_batch2(cuda_device):
     labels = np.array([[1, 0, 0, 1], [0, 0, 0, 1]], dtype=np.float64)
-    errs = _run_both("bf16", 28, 4, labels, [200, 77], 4, 128, 256, seed=22, batch=2)
+    errs = ge.run_both("bf16", 28, 4, labels, [200, 77], 4, 128, 256, seed=22, batch=2)
     assert max(errs.values()) <= 2e-2, errs
 
 
@@ -69,7 +45,7 @@ def test_split_kv_prefill_against_oracle(cuda_device, Hq, labels_row):
     ranges are empty), then short chunks over a long cache; group sizes 4 (head
     pairs) and 7 (pairs plus a single-head CTA)."""
     labels = np.array([labels_row], dtype=np.float64)
-    errs = _run_both("bf16", Hq, 2, labels, [3000, 2500, 256, 200, 129], 2, 128, 256, seed=24)
+    errs = ge.run_both("bf16", Hq, 2, labels, [3000, 2500, 256, 200, 129], 2, 128, 256, seed=24)
     assert max(errs.values()) <= 2e-2, errs
 
 
@@ -77,14 +53,14 @@ def test_split_kv_prefill_against_oracle(cuda_device, Hq, labels_row):
 def test_window_edge_cases(cuda_device, sink, recent):
     labels = np.array([[0, 1]], dtype=np.float64)
     for dtype in ("f32", "bf16"):
-        errs = _run_both(dtype, 8, 2, labels, [37, 64, 5], 6, sink, recent, seed=23)
+        errs = ge.run_both(dtype, 8, 2, labels, [37, 64, 5], 6, sink, recent, seed=23)
         assert max(errs.values()) <= gc.TOL[dtype], (dtype, errs)
 
 
 def test_decode_from_empty_cache(cuda_device):
     # past_len = 0: every head attends to the new key only
     labels = np.array([[1, 0]], dtype=np.float64)
-    errs = _run_both("bf16", 8, 2, labels, [], 3, 128, 256, seed=24)
+    errs = ge.run_both("bf16", 8, 2, labels, [], 3, 128, 256, seed=24)
     assert errs["decode"] <= 2e-2
 
 

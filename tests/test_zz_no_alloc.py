@@ -66,3 +66,50 @@ def test_noalloc_rejects_layers_beyond_its_scratch(cuda_device):
                                            C.c_void_p(_lib.stream_handle()))
     assert rc == _lib.UNSUPPORTED
     assert b"static scratch" in _lib.lib().aoh_last_error()
+
+
+def test_noalloc_partitioned_cache_and_device_length(cuda_device):
+    """A cache holding only some units (one rank's share of the multi-GPU
+    partition, no peers attached), decoded with the length read from the
+    device (AOH_PAST_LEN_DEVICE, the mode a replayed decode step uses): the
+    owned heads match aoh_attn_decode on the same cache contents, on two
+    consecutive steps."""
+    Hq, G, B, T = 28, 4, 2, 9000
+    grp = Hq // G
+    labels = np.array([[1, 0, 1, 0]], dtype=np.float64)
+    owned = np.zeros((1, B, G), dtype=np.uint8)
+    owned[0, 0, [0, 1]] = 1  # sequence 0: a retrieval and a streaming group
+    owned[0, 1, [2]] = 1     # sequence 1: a retrieval group
+    gen = torch.Generator(device="cuda").manual_seed(43)
+    kw = dict(batch=B, max_context=T + 4, dtype=torch.bfloat16, owned=owned, reserve_all=True)
+    ref = AoHKVCache(labels, Hq, **kw)
+    tst = AoHKVCache(labels, Hq, **kw)
+    pv = ref.pool_view()
+    pv.copy_((torch.randn(pv.shape, generator=gen, device="cuda") * 0.5).to(torch.bfloat16))
+    tst.pool.copy_(ref.pool)
+    lib = _lib.lib()
+    st = C.c_void_p(_lib.stream_handle())
+    _lib.check(lib.aoh_kv_set_length(tst._h, T, st), "aoh_kv_set_length")
+    ws = ref.decode_workspace()
+    for step in range(2):
+        q = torch.randn((B, 1, Hq, 128), generator=gen, device="cuda").to(torch.bfloat16)
+        k = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+        v = (torch.randn((B, 1, G, 128), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+        want = torch.full_like(q, float("nan"))
+        got = torch.full_like(q, float("nan"))
+        _lib.check(lib.aoh_attn_decode(ref._h, 0, T + step, _p(q), _p(k), _p(v), _p(want), _p(ws), ws.numel(), st),
+                   "aoh_attn_decode")
+        _lib.check(lib.aoh_attn_decode_noalloc(tst._h, 0, _lib.PAST_LEN_DEVICE, _p(q), _p(k), _p(v), _p(got), st),
+                   "aoh_attn_decode_noalloc")
+        _lib.check(lib.aoh_kv_advance(tst._h, 1, st), "aoh_kv_advance")
+        torch.cuda.synchronize()
+        for b in range(B):
+            for g in range(G):
+                heads = slice(g * grp, (g + 1) * grp)
+                if owned[0, b, g]:
+                    assert torch.isfinite(got[b, :, heads].float()).all()
+                    assert torch.allclose(got[b, :, heads].float(), want[b, :, heads].float(), atol=2e-2, rtol=0)
+                else:  # units stored elsewhere are not computed here
+                    assert torch.isnan(got[b, :, heads].float()).all()
+    assert ref.device_status() == 0 and tst.device_status() == 0
+    assert torch.equal(ref.pool, tst.pool)
