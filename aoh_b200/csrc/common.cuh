@@ -111,6 +111,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return mbar_wait_slow(bar, parity, err);
 }
 
+// Bounded wait for copies that other CTAs write into this CTA's shared memory:
+// it does not give up early when another wait has tripped (those CTAs still
+// send their copies once their own waits give up, and this CTA must not exit
+// before the copies land), only after kPeerWaitNs.
+__device__ __forceinline__ bool mbar_wait_incoming(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kPeerWaitNs) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // Per-thread register budget of the executing warpgroup (all 128 threads run
 // it together); increases wait until other warpgroups have released enough of
 // the registers the block was launched with.
@@ -297,6 +315,23 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync_all, for a barrier whose wait comes much later.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Bulk copy from this CTA's shared memory into the shared memory of a CTA of
+// the cluster (dst and the mbarrier are shared::cluster addresses from
+// mapa_shared); completion is signalled on that CTA's mbarrier.  16-byte
+// aligned, size a multiple of 16.  A plain one-to-one copy inside this GPU.
+__device__ __forceinline__ void bulk_store_cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk copy of this thread has finished reading its source.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // Shared-memory address of `p` (this CTA) in the CTA of rank `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {

@@ -67,7 +67,9 @@ constexpr int kMaxSplit = 1024;
 constexpr int kPartialFloats = kMaxGrp * kHeadDim + 2 * kMaxGrp;
 constexpr int kOPitch = kHeadDim + 4;  // padded row of the warp-merge scratch
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
-constexpr int kCounterBytes = kMaxUnits * 4;
+// Workspace tickets: per (unit, cluster slice) one ticket, then per unit one
+// count of stored slices (multi-GPU publish); all zero between launches.
+constexpr int kCounterBytes = kMaxUnits * (8 + 1) * 4;
 constexpr int kCluster = 8;
 static_assert(kMaxGrp * kHeadDim / kCluster <= kThreads, "a cluster CTA's output slice is one element per thread");
 
@@ -89,7 +91,7 @@ struct DecodeArgs {
   const int* T_dev;  // if non-null, past_len is read from here (CUDA-graph replay)
   float scale_log2;  // D^-0.5 * log2(e)
   float* ws;         // per-cluster partials, (kMaxCtas / kCluster) x kPartialFloats
-  int* counters;     // kMaxUnits tickets, zero between launches
+  int* counters;     // [unit][slice] tickets, then [unit] stored-slice counts; zero between launches
   // 0: the kernel before this one in the stream wrote this layer's pages
   // (e.g. a prefill chunk's append), so no page is streamed before waiting
   // for it; 1: only the page of position T-1 may still be in flight
@@ -574,74 +576,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[kMaxGrp * kHeadDim + kMaxGrp + qq] = L;
       }
     }
-    // The cluster barrier orders every CTA's partial stores before rank 0's
-    // ticket; the ticket is an acq_rel atomic at GPU scope, cumulative over
-    // them (release) and, for the last cluster, over every other cluster's
-    // partial (acquire), which the next cluster barrier extends to its CTAs.
-    cluster_sync_all();  // the cluster's partial is complete; no DSMEM reads after this
-    if (rank == 0 && tid == 0) {
-      int ticket;
-      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(ticket) : "l"(&a.counters[u]) : "memory");
-      const uint32_t last = ticket == nk - 1;
-      for (int c = 0; c < kCluster; ++c) st_dsmem_u32(mapa_shared((const void*)&s_last, c), last);
-    }
+    // The cluster barrier orders every CTA's slice stores before that CTA's
+    // ticket for its slice, an acq_rel atomic at GPU scope: cumulative over
+    // them (release) and, for the last cluster to store the slice, over every
+    // other cluster's slice (acquire), which __syncthreads extends to the CTA.
+    // No CTA reads another's shared memory after this barrier.
     cluster_sync_all();
+    if (tid == 0) {
+      int ticket;
+      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                   : "=r"(ticket)
+                   : "l"(&a.counters[u * kCluster + rank])
+                   : "memory");
+      s_last = ticket == nk - 1;
+    }
+    __syncthreads();
     if (!s_last) return;
-    // ============ last cluster of the unit: combine its nk partials, 1/8 of outputs per CTA ============
-    // this thread's element of the first 16 partials, in flight while the weights are formed
-    // (a CTA's slice is at most kThreads elements: one per thread)
-    const int e_mine = e_lo + tid;
-    float v_first[16];
+    // ============ the last cluster to store slice `rank` combines it over the unit's nk partials ============
+    // This thread's element of up to 32 partials is loaded with the slice rows'
+    // m and l, in one round of loads; more partials are read as they are used.
+    const int e_mine = e_lo + tid;  // a CTA's slice is at most kThreads elements: one per thread
+    const bool mine = e_mine < e_hi;
+    constexpr int kPre = 32;
+    float v[kPre];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      v_first[j] = (e_mine < e_hi && j < nk) ? __ldcg(parts + e_mine + (size_t)j * kPartialFloats) : 0.f;
-    // weights w[k][q] = exp2(m_k - M_q) / L_q in shared memory (the stage ring is free)
-    float* sw = reinterpret_cast<float*>(smem);      // [nk][kMaxGrp]
-    float* sml = sw + kMaxSplit / kCluster * kMaxGrp;  // [nk][kMaxGrp][2] raw (m, l)
-    for (int i = tid; i < nk * grp; i += kThreads) {
-      const int k = i / grp, qq = i % grp;
-      const float* pk = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim;
-      sml[(k * kMaxGrp + qq) * 2] = __ldcg(pk + qq);
-      sml[(k * kMaxGrp + qq) * 2 + 1] = __ldcg(pk + kMaxGrp + qq);
+    for (int j = 0; j < kPre; ++j)
+      v[j] = (mine && j < nk) ? __ldcg(parts + e_mine + (size_t)j * kPartialFloats) : 0.f;
+    const int q_lo = e_lo >> 7, n_rows = ((e_hi - 1) >> 7) - q_lo + 1;  // the slice spans one or two rows
+    float* sml = reinterpret_cast<float*>(smem);                         // [row][k][m, l] (the ring is free)
+    for (int i = tid; i < nk * n_rows; i += kThreads) {
+      const int r = i / nk, k = i % nk;
+      const float* pm = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + q_lo + r;
+      sml[(r * (kMaxSplit / kCluster) + k) * 2] = __ldcg(pm);
+      sml[(r * (kMaxSplit / kCluster) + k) * 2 + 1] = __ldcg(pm + kMaxGrp);
     }
     __syncthreads();
-    for (int qq = warp; qq < grp; qq += kThreads / 32) {
+    if (mine) {
+      const float* ml = sml + ((e_mine >> 7) - q_lo) * (kMaxSplit / kCluster) * 2;
       float M = -INFINITY;
-      for (int k = lane; k < nk; k += 32) M = fmaxf(M, sml[(k * kMaxGrp + qq) * 2]);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      for (int k = 0; k < nk; ++k) M = fmaxf(M, ml[2 * k]);
       const float Mu = M == -INFINITY ? 0.f : M;
-      float L = 0.f;
-      for (int k = lane; k < nk; k += 32) {
-        const float f = fast_exp2(sml[(k * kMaxGrp + qq) * 2] - Mu);
-        sw[k * kMaxGrp + qq] = f;
-        L += sml[(k * kMaxGrp + qq) * 2 + 1] * f;
+      float acc = 0.f, L = 0.f;
+#pragma unroll
+      for (int j = 0; j < kPre; ++j) {
+        if (j < nk) {
+          const float f = fast_exp2(ml[2 * j] - Mu);
+          acc += v[j] * f;
+          L += ml[2 * j + 1] * f;
+        }
       }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      const float inv = 1.f / L;
-      __syncwarp();
-      for (int k = lane; k < nk; k += 32) sw[k * kMaxGrp + qq] *= inv;
-    }
-    __syncthreads();
-    if (e_mine < e_hi) {
-      const int e = e_mine;
-      const int qq = e >> 7;
-      const float* po = parts + e;  // partial k's output e at po[k * kPartialFloats]
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < nk) acc[j & 3] += v_first[j] * sw[j * kMaxGrp + qq];
-      int k = 16;
-      for (; k + 16 <= nk; k += 16) {
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __ldcg(po + (size_t)(k + j) * kPartialFloats);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j & 3] += v[j] * sw[(k + j) * kMaxGrp + qq];
+      for (int k = kPre; k < nk; ++k) {
+        const float f = fast_exp2(ml[2 * k] - Mu);
+        acc += __ldcg(parts + e_mine + (size_t)k * kPartialFloats) * f;
+        L += ml[2 * k + 1] * f;
       }
-      for (; k < nk; ++k) acc[0] += __ldcg(po + (size_t)k * kPartialFloats) * sw[k * kMaxGrp + qq];
-      s_out[tid] = __float2bfloat16((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      s_out[tid] = __float2bfloat16(acc / L);
     }
     __syncthreads();
     // the slice (grp * 16 elements, starting at a multiple of 8) leaves as 16-byte stores
@@ -649,11 +638,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_out8(a, out_u + e_lo + 8 * c, reinterpret_cast<const uint4*>(s_out)[c]);
     // the ticket is reset before the unit is published: once every unit of the
     // layer is published, the next kernel may reuse the workspace
-    if (rank == 0 && tid == 0) a.counters[u] = 0;
+    if (tid == 0) a.counters[u * kCluster + rank] = 0;
     if (a.n_ranks > 0) {
-      cluster_sync_all();  // every CTA of the cluster stored its slice of the unit
-      if (rank == 0 && tid == 0) publish_unit(a, bg, T);
+      // the finisher of the unit's last stored slice publishes it (its acquire
+      // covers the other slices' stores, its system-scope fence all of them)
+      __syncthreads();  // this slice is stored in every rank's region
+      if (tid == 0) {
+        int* done = a.counters + kMaxUnits * kCluster + u;
+        int n;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(n) : "l"(done) : "memory");
+        if (n == kCluster - 1) {
+          *done = 0;
+          publish_unit(a, bg, T);
+        }
+      }
     }
+    // the last cluster to store slice 0 follows every cluster of the unit past
+    // its main loop: it appends the new token
     if (rank != 0) return;
   }
 
@@ -857,7 +858,7 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
 // For callers that cannot allocate device memory (see include/aoh.h), the
 // decode workspace lives in a file-scope device array instead of a
 // caller-provided buffer.  It holds the per-unit tickets and up to
-// kNoAllocClusters cluster partials: 1 KB + 64 x 4160 B = 267,264 bytes, which
+// kNoAllocClusters cluster partials: 9 KB + 64 x 4160 B = 275,456 bytes, which
 // every GPU that loads this library keeps until the process exits.  The array
 // is shared by every call: calls that overlap on the GPU race on it.
 // ---------------------------------------------------------------------------

@@ -183,7 +183,7 @@ AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len
  * reachable from the calling layer).  No counterpart in the reference, whose
  * eager path allocates new tensors on every call.
  *
- * The split-KV scratch is a static device array inside libaoh.so: 267,264
+ * The split-KV scratch is a static device array inside libaoh.so: 275,456
  * bytes (tickets for 256 units + 64 cluster partials), held on every GPU that
  * loads the library until the process exits.  bf16 caches only; a layer whose
  * plan would need more than 256 (sequence, KV head) units or more than 64
