@@ -195,6 +195,25 @@ __device__ __forceinline__ int append_slot(const UnitView& uv, int pos, int* j) 
   return r % kPage;
 }
 
+// One warp writes the new token's K and V rows (position T) into their page
+// slot: lanes 0-15 K, 16-31 V, 16 bytes each, in the pre-swizzled layout.
+__device__ __forceinline__ void append_token(const DecodeArgs& a, const UnitView& uv, const int32_t* bt, int b, int g,
+                                             int lane) {
+  const CacheGeom& G = a.geom;
+  int j = 0;
+  const int slot = append_slot(uv, uv.T, &j);
+  if (slot < 0) return;
+  const int pid = bt[j];
+  if (pid < 0 || pid >= G.num_pages) {
+    if (lane == 0) atomicOr(G.err, kErrBadPage);
+    return;
+  }
+  const int kv = lane >> 4, c8 = lane & 15;
+  const __nv_bfloat16* src = (kv ? a.v_new : a.k_new) + ((size_t)b * G.G + g) * kHeadDim;
+  uint8_t* dst = static_cast<uint8_t*>(G.pool) + (size_t)pid * kPageBf16Bytes + bf16_chunk_offset(kv, slot, c8);
+  *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(src)[c8];
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     decode_bf16_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodePlan plan) {
   extern __shared__ uint8_t smem_raw[];
@@ -318,6 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // already started streaming this layer's pages, which it does not write).
     griddep_wait();
     if (tid == 32) griddep_launch_dependents();
+    // A retrieval unit's new token goes to the slot of position T, which no CTA
+    // of this launch attends (every cached key it reads is below T, and a torn
+    // read of that slot is masked like any unattended slot), so the unit's
+    // first CTA writes it now, off the end of the kernel.
+    if (retr && split == 0 && cw == 0) append_token(a, uv, bt, b, g, lane);
     // Q^T B-fragments: qf[kk][0] = Q[n][16kk+2c..+1], qf[kk][1] = Q[n][16kk+8+2c..+1], n = lane/4
     uint32_t qf[8][2];
     {
@@ -576,12 +600,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[kMaxGrp * kHeadDim + kMaxGrp + qq] = L;
       }
     }
-    // The cluster barrier orders every CTA's slice stores before that CTA's
-    // ticket for its slice, an acq_rel atomic at GPU scope: cumulative over
-    // them (release) and, for the last cluster to store the slice, over every
-    // other cluster's slice (acquire), which __syncthreads extends to the CTA.
-    // No CTA reads another's shared memory after this barrier.
-    cluster_sync_all();
+    // This CTA's reads of the cluster's shared memory are done: it arrives now
+    // and waits only before leaving (no CTA exits while another may still read
+    // its partial), so the ticket and the combine overlap the slower members.
+    cluster_arrive();
+    // __syncthreads orders every thread's slice stores before the ticket, an
+    // acq_rel atomic at GPU scope: cumulative over them (release) and, for the
+    // last cluster to store the slice, over every other cluster's slice
+    // (acquire), which the next __syncthreads extends to the CTA.
+    __syncthreads();
     if (tid == 0) {
       int ticket;
       asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
@@ -591,7 +618,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_last = ticket == nk - 1;
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+      cluster_wait();
+      return;
+    }
     // ============ the last cluster to store slice `rank` combines it over the unit's nk partials ============
     // This thread's element of up to 32 partials is loaded with the slice rows'
     // m and l, in one round of loads; more partials are read as they are used.
@@ -653,27 +683,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    cluster_wait();
     // the last cluster to store slice 0 follows every cluster of the unit past
-    // its main loop: it appends the new token
-    if (rank != 0) return;
+    // its main loop: a split streaming unit's new token goes in now (its ring
+    // slot may hold a key this launch attends)
+    if (rank != 0 || retr) return;
   }
 
-  // ===================== append the new token (after every read of the unit) =====================
-  if (tid < 32) {
-    int j = 0;
-    const int slot = append_slot(uv, T, &j);
-    if (slot >= 0) {
-      const int pid = bt[j];
-      if (pid < 0 || pid >= G.num_pages) {
-        if (tid == 0) atomicOr(G.err, kErrBadPage);
-      } else {
-        const int kv = tid >> 4, c8 = tid & 15;  // 16 lanes x 16 B per row
-        const __nv_bfloat16* src = (kv ? a.v_new : a.k_new) + ((size_t)b * G.G + g) * kHeadDim;
-        uint8_t* dst = static_cast<uint8_t*>(G.pool) + (size_t)pid * kPageBf16Bytes + bf16_chunk_offset(kv, slot, c8);
-        *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(src)[c8];
-      }
-    }
-  }
+  // ===================== a streaming unit's new token (after every read of the unit) =====================
+  if (!retr && tid < 32) append_token(a, uv, bt, b, g, lane);
 }
 
 // CTAs resident at once when launched in clusters of kCluster, per device
