@@ -74,6 +74,7 @@ _SIGNATURES = {
     "aoh_shared_close": (C.c_int, [_vp]),
     "aoh_kv_set_peers": (C.c_int, [_vp, _i32, _i32, C.POINTER(_vp), C.c_size_t, C.POINTER(_vp)]),
     "aoh_gather_wait": (C.c_int, [_vp, _i32, _i32, _vp]),
+    "aoh_diag_exp2_poly": (C.c_int, [_vp, _vp, _i32, _vp]),
 }
 IPC_HANDLE_BYTES = 64
 

@@ -40,22 +40,20 @@ def save_results(output_dir: str, eff_ranks_q: np.ndarray, eff_ranks_kv: np.ndar
     os.replace(tmp, out / "results.json")
 
 
+# result key -> file name: the reference's names, so head maps move between the two
+_FILES = (("eff_ranks_q", "eff_rank.npy"), ("eff_ranks_kv", "eff_rank_kv.npy"),
+          ("head_labels", "head_classification.npy"), ("metadata", "results.json"))
+
+
 def load_results(output_dir: str) -> dict:
+    """The four head-map files of ``output_dir`` as a dict (arrays, and the
+    run metadata from results.json).  FileNotFoundError, as in the reference,
+    when any of them is absent -- naming every absent one."""
     out = Path(output_dir)
-    required = {
-        "eff_ranks_q": out / "eff_rank.npy",
-        "eff_ranks_kv": out / "eff_rank_kv.npy",
-        "head_labels": out / "head_classification.npy",
-        "metadata": out / "results.json",
-    }
-    missing = [p.name for p in required.values() if not p.exists()]
-    if missing:
-        raise FileNotFoundError(f"Missing AoH result files in {out}: {', '.join(sorted(missing))}")
-    with required["metadata"].open(encoding="utf-8") as f:
-        metadata = json.load(f)
-    return {
-        "eff_ranks_q": np.load(required["eff_ranks_q"]),
-        "eff_ranks_kv": np.load(required["eff_ranks_kv"]),
-        "head_labels": np.load(required["head_labels"]),
-        "metadata": metadata,
-    }
+    paths = {key: out / name for key, name in _FILES}
+    absent = sorted(name for key, name in _FILES if not paths[key].is_file())
+    if absent:
+        raise FileNotFoundError(f"{out} is not a complete head map: no {', '.join(absent)}")
+    loaded = {key: np.load(path) for key, path in paths.items() if key != "metadata"}
+    loaded["metadata"] = json.loads(paths["metadata"].read_text(encoding="utf-8"))
+    return loaded

@@ -920,6 +920,8 @@ def main():
                     help="only the whole-model decode ms/token (random-init Llama-3.1-8B, --context tokens)")
     ap.add_argument("--prefill-full", type=int, default=0, metavar="CHUNK",
                     help="only the full 64K chunked prefill at this chunk size")
+    ap.add_argument("--classifier-only", action="store_true",
+                    help="only the classifier on the Qwen2.5-7B-shaped projections (labels, timing)")
     ap.add_argument("--context", type=int, default=0, help="cached tokens (profiling cases; default: the workload's)")
     ap.add_argument("--layers", type=int, default=0, help="layers (profiling cases; default: the workload's)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=MAIN,
@@ -932,7 +934,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.prefill_only or args.whole_model or args.prefill_full:
+    if args.prefill_only or args.whole_model or args.prefill_full or args.classifier_only:
         import torch
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
@@ -941,6 +943,8 @@ def main():
             res = {"prefill": prefill_sample(torch, dev, peaks)}
         elif args.whole_model:
             res = {"whole_model": whole_model(torch, dev, context=args.context or 131072)}
+        elif args.classifier_only:
+            res = {"labels_exact": classifier_block(torch, dev)}
         else:
             res = {"prefill": prefill_full(torch, dev, peaks, args.prefill_full)}
         print(json.dumps(res), flush=True)

@@ -288,6 +288,16 @@ AOH_API int aoh_kv_set_peers(aoh_kv_cache* cache, int32_t n_ranks, int32_t rank,
  * cache's device check word (aoh_kv_device_status) instead of hanging. */
 AOH_API int aoh_gather_wait(aoh_kv_cache* cache, int32_t layer, int32_t past_len, aoh_stream stream);
 
+/* ------------------------------------------------------------------------- */
+/* Diagnostics (no counterpart in the reference): one building block of the  */
+/* kernels on caller-given device data, for tests.                           */
+/* ------------------------------------------------------------------------- */
+
+/* out[i] = 2^x[i] as the prefill softmax computes it on the FMA pipe (a cubic
+ * on the fraction, the integer part added to the exponent; x in [-126, 8]);
+ * x and out: device float32 arrays of n elements. */
+AOH_API int aoh_diag_exp2_poly(const float* x, float* out, int32_t n, aoh_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

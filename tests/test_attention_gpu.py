@@ -273,3 +273,31 @@ def test_prefill_partitioned_cache(cuda_device):
             kk, vv = part.read_rows(0, seq, g, pos)
             assert torch.equal(kk, k[seq, pos, g]) and torch.equal(vv, v[seq, pos, g]), (c, seq, g)
     assert part.device_status() == 0 and full.device_status() == 0
+
+
+def test_softmax_exp2_polynomial(cuda_device):
+    """The prefill softmax computes 3 of every 8 exponentials with a cubic on
+    the FMA pipe instead of the MUFU.  Against an exact float64 2^x: over
+    [-125, 8] its relative error stays below 7.6e-5 -- under half a bf16 ulp
+    of P, which is rounded to bf16 next -- and the bf16 rounding of its result
+    is within one bf16 ulp of the rounded exact value; below -125, where the
+    result sits at the bottom of the normal range (x is clamped to -126), the
+    absolute error stays under 2^-138, nothing next to a row sum of at least 1."""
+    import ctypes as C
+
+    from aoh_b200 import _lib
+    xs = np.concatenate([np.linspace(-126.0, 8.0, 2_000_001), np.arange(-126, 9, dtype=np.float64),
+                         np.arange(-126, 8, dtype=np.float64) + 0.5]).astype(np.float32)
+    x = torch.from_numpy(xs).cuda()
+    out = torch.empty_like(x)
+    _lib.check(_lib.lib().aoh_diag_exp2_poly(C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()), x.numel(),
+                                             C.c_void_p(_lib.stream_handle())), "aoh_diag_exp2_poly")
+    got = out.cpu().numpy().astype(np.float64)
+    want = np.exp2(xs.astype(np.float64))
+    m = xs >= -125
+    rel = np.abs(got[m] - want[m]) / want[m]
+    assert rel.max() < 7.6e-5, (float(rel.max()), float(xs[m][np.argmax(rel)]))
+    assert np.abs(got[~m] - want[~m]).max() < 2.0 ** -138
+    gb = syn.bf16_round(got[m].astype(np.float32)).astype(np.float64)
+    wb = syn.bf16_round(want[m].astype(np.float32)).astype(np.float64)
+    assert np.all(np.abs(gb - wb) <= np.spacing(wb.astype(np.float32)).astype(np.float64) * 65536)

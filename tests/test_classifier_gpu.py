@@ -1,10 +1,13 @@
 """GPU effective ranks and labels against the reference's outputs.
 
 Effective ranks: within 1e-4 relative (observed ~1e-6: the reference's own
-float32 eigvals noise).  Labels: every decision whose boundary gap exceeds the
-reference's float32 noise floor must match bit for bit; decisions inside that
-floor (exact float32 ties of aggregated ranks) are listed, since no arithmetic
-other than the reference's own LAPACK build reproduces its rounding there."""
+float32 eigvals noise).  Labels: every layer decision matches the reference's
+bit for bit, except where the reference's own float32 ranks tie at the
+retrieval/streaming boundary (gap within a few float32 ulps): there its label
+is decided by its LAPACK build's rounding, which no other arithmetic
+reproduces.  For the seed-0 Qwen2.5-7B-shaped case those decisions are pinned
+exactly; for four more seeds each differing decision's gap is bounded and
+printed."""
 import ast
 
 import numpy as np
@@ -16,7 +19,6 @@ from aoh_b200 import synthetic as syn
 from tests.golden_cases import GOLDEN
 
 pytestmark = pytest.mark.gpu
-NOISE_FLOOR = 2e-6  # relative; 2x the largest reference-vs-exact rank error seen
 
 
 def _weights(spec):
@@ -29,29 +31,57 @@ def _weights(spec):
     return torch.stack(wq).cuda(), torch.stack(wk).cuda()
 
 
-@pytest.mark.parametrize("name", ["cls_small", "cls_qwen25_7b"])
+# The decisions of the seed-0 Qwen2.5-7B-shaped case that differ from the
+# reference's: --binary mode, max aggregation, where the reference's own
+# aggregated ranks tie in float32 at the retrieval/streaming boundary.
+KNOWN_FLIPS = {"cls_qwen25_7b": {("binary", "max", 0.5, 12), ("binary", "max", 0.75, 9), ("binary", "max", 0.75, 12)}}
+MAX_TIE_ULPS = 16  # about the reference's own float32 eigvals noise (1e-6 relative)
+
+
+def boundary_ulps(kv_ranks: np.ndarray, sparsity: float) -> np.ndarray:
+    """Per layer, the gap between the highest-ranked retrieval KV head and the
+    lowest-ranked streaming one (the decision the label rests on) in float32
+    ulps of the ranks; inf when every head has the same label."""
+    L, G = kv_ranks.shape
+    k = max(0, min(G, round((1.0 - sparsity) * G)))
+    out = np.full(L, np.inf)
+    if 0 < k < G:
+        r = np.sort(kv_ranks, axis=1)
+        out = (r[:, k] - r[:, k - 1]) / np.spacing(np.abs(r[:, k - 1]).astype(np.float32)).astype(np.float64)
+    return out
+
+
+@pytest.mark.parametrize("name", ["cls_small", "cls_qwen25_7b"] + [f"cls_qwen25_7b_s{s}" for s in (1, 2, 3, 4)])
 @pytest.mark.parametrize("mode", ["fp32", "binary"])
 def test_eff_ranks_and_labels(cuda_device, name, mode):
-    z = np.load(GOLDEN / f"{name}.npz")
+    """Ranks within 1e-4 relative of the reference's; every layer decision equal
+    to the reference's except where the reference's own float32 ranks tie at
+    the boundary (within MAX_TIE_ULPS) -- and, for the seed-0 case, exactly the
+    known three."""
+    path = GOLDEN / f"{name}.npz"
+    if not path.exists():
+        pytest.skip(f"{name} fixture not generated")
+    z = np.load(path)
     spec = ast.literal_eval(str(z["spec"]))
     wq, wk = _weights(spec)
     ranks = clf.eff_ranks_from_weights(wq, wk, spec["Hq"], spec["G"], spec["D"], binary=(mode == "binary"))
     ref = z[f"{mode}_eff_ranks_q"]
     assert np.all(np.abs(ranks - ref) <= 1e-4 * np.abs(ref))
     assert np.array_equal(ranks, ranks.astype(np.float32).astype(np.float64))  # float(fp32) values
-    sub_noise = []
+    flips = {}
     for agg in ("mean", "min", "max"):
         kv = clf.aggregate_kv(ranks, spec["G"], agg)
         for sp in (0.25, 0.5, 0.75):
             lab = clf.labels_from_ranks(kv, sp)
             want = z[f"{mode}_{agg}_sp{sp}_labels"]
-            margins = clf.label_margins(kv, sp)
+            ulps = boundary_ulps(z[f"{mode}_{agg}_eff_ranks_kv"], sp)
             for l in np.where((lab != want).any(axis=1))[0]:
-                assert margins[l] < NOISE_FLOOR, (agg, sp, l, margins[l])
-                sub_noise.append((agg, sp, int(l), float(margins[l])))
-    if mode == "fp32":
-        assert not sub_noise, sub_noise  # every float32-mode label matches the reference
-    assert len(sub_noise) <= 6, sub_noise
+                flips[(mode, agg, sp, int(l))] = float(ulps[l])
+    print(f"{name} {mode}: differing decisions (reference boundary gap in float32 ulps): {flips}")
+    for key, gap in flips.items():
+        assert gap <= MAX_TIE_ULPS, (key, gap)
+    if name in KNOWN_FLIPS:
+        assert set(flips) == {f for f in KNOWN_FLIPS[name] if f[0] == mode}, flips
 
 
 def test_classifier_api_on_stub_model(cuda_device):
