@@ -35,7 +35,10 @@ def _weights(spec):
 # reference's: --binary mode, max aggregation, where the reference's own
 # aggregated ranks tie in float32 at the retrieval/streaming boundary.
 KNOWN_FLIPS = {"cls_qwen25_7b": {("binary", "max", 0.5, 12), ("binary", "max", 0.75, 9), ("binary", "max", 0.75, 12)}}
-MAX_TIE_ULPS = 16  # about the reference's own float32 eigvals noise (1e-6 relative)
+# The reference's float32 ranks deviate from exact ones by up to 1.3e-6 relative
+# (measured against a float64 solve), so two of them closer than about twice
+# that -- 22 float32 ulps -- can be ordered either way by its own rounding.
+MAX_TIE_ULPS = 24
 
 
 def boundary_ulps(kv_ranks: np.ndarray, sparsity: float) -> np.ndarray:
