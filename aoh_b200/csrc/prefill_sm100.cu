@@ -119,6 +119,12 @@ struct PrefillArgs {
   int prefetch;
   uint8_t* ws;
   int* counters;  // one per (retrieval item, row block), zero between launches
+  // coop: the whole grid is one wave (every split of a row block resident at
+  // once), so each split waits for all partials of its row block and combines
+  // its own share of the rows; done counts the splits that finished combining
+  // (zero between launches).  Otherwise the last split to arrive combines all.
+  int coop;
+  int* done;
   // Append: the kernel writes this call's k/v rows to the layer's pages.
   // Retrieval units: warp 11 of the group's two-head CTAs (of its one-head
   // CTAs when the group has a single head) copies a share of its row block
@@ -232,6 +238,28 @@ struct TileList {
     return r0 >= lo && r0 + BN <= min(hi, min(C, i0q + BM)) && r0 + BN - 1 <= i0q;
   }
 };
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *count reaches target (other CTAs of this grid, all
+// resident, increment it): false after kWaitNs, or once another wait tripped.
+__device__ __forceinline__ bool wait_count(const int* count, int target, int* err) {
+  if (ld_acquire_gpu(count) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (ld_acquire_gpu(count) >= target) return true;
+    if (wait_tripped(err)) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+    __nanosleep(32);
+  }
+}
 
 __device__ __forceinline__ uint8_t* align1024p(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -759,6 +787,79 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       pml[row] = have ? m_used : -INFINITY;
       pml[BM + row] = have ? l : 0.f;
+      if (a.coop) {
+        // Every split of this row block is resident: each announces its partial
+        // (a release add after the barrier, cumulative over the CTA's partial
+        // stores), waits until all have (acquire), and combines its own share of
+        // the rows -- 8 dims x one row per thread and item, the splits' m, l and
+        // values loaded in batches, the running maximum rescaling the sums.
+        named_bar_sync(3, nq * 128);
+        if (tid == 0) {
+          asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(&a.counters[gslot]) : "memory");
+          if (!wait_count(&a.counters[gslot], n_split, G.err)) s_abort = 1;
+        }
+        named_bar_sync(3, nq * 128);
+        const int r_lo = BM * split / n_split, r_hi = BM * (split + 1) / n_split;
+        const int per_tile = (r_hi - r_lo) * (kHeadDim / 8);
+        for (int it = tid; it < nq * per_tile; it += nq * 128) {
+          const int qq = it / per_tile, rem = it - qq * per_tile;
+          const int r = r_lo + rem / (kHeadDim / 8), c8 = rem % (kHeadDim / 8);
+          const uint8_t* p0 = a.ws + ((size_t)gslot * n_split * 2 + qq) * kPartBytes;  // split s at + s * 2 * kPartBytes
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float M = -INFINITY, L = 0.f;
+          constexpr int kB = 8;
+          for (int sp = 0; sp < n_split; sp += kB) {
+            uint4 v[kB];
+            float ms[kB], ls[kB];
+#pragma unroll
+            for (int k = 0; k < kB; ++k) {
+              ms[k] = -INFINITY;
+              ls[k] = 0.f;
+              v[k] = make_uint4(0u, 0u, 0u, 0u);
+              if (sp + k < n_split) {
+                const uint8_t* ps = p0 + (size_t)(sp + k) * 2 * kPartBytes;
+                const float* qml = reinterpret_cast<const float*>(ps + BM * kHeadDim * 2);
+                ms[k] = __ldcg(qml + r);
+                ls[k] = __ldcg(qml + BM + r);
+                v[k] = __ldcg(reinterpret_cast<const uint4*>(ps) + c8 * BM + r);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < kB; ++k) {
+              if (!(ls[k] > 0.f)) continue;  // an empty range (or none): no keys for this row
+              const float Mn = fmaxf(M, ms[k]);
+              const float alpha = fast_exp2(M - Mn);
+              const float w = fast_exp2(ms[k] - Mn) * ls[k];
+              L = fmaf(L, alpha, w);
+              const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = fmaf(w, bf16_lo(u[j]), acc[2 * j] * alpha);
+                acc[2 * j + 1] = fmaf(w, bf16_hi(u[j]), acc[2 * j + 1] * alpha);
+              }
+              M = Mn;
+            }
+          }
+          const int qi_r = q_row0(qq) + r;
+          if (qi_r < a.C) {
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            __nv_bfloat16* d = a.out + (((size_t)b * a.C + qi_r) * G.Hq + q_head(qq)) * kHeadDim + 8 * c8;
+            *reinterpret_cast<uint4*>(d) =
+                make_uint4(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv),
+                           pack_bf16(acc[4] * inv, acc[5] * inv), pack_bf16(acc[6] * inv, acc[7] * inv));
+          }
+        }
+        // the last split to finish combining makes both counters ready for the next launch
+        named_bar_sync(3, nq * 128);
+        if (tid == 0) {
+          int t;
+          asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(t) : "l"(&a.done[gslot]) : "memory");
+          if (t == n_split - 1) {
+            a.counters[gslot] = 0;
+            a.done[gslot] = 0;
+          }
+        }
+      } else {
       // The barrier orders every thread's partial stores before the ticket, an
       // acq_rel atomic at GPU scope: cumulative over those stores (release),
       // and, for the last split, over the other splits' partials (acquire).
@@ -820,6 +921,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           store_half(acc, hlf, L > 0.f ? 1.f / L : 0.f);
         }
         if (tid == 0) a.counters[gslot] = 0;  // ready for the next launch
+      }
       }
     }
     if (!retr) {
@@ -968,7 +1070,10 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   // ranges so that the heavy CTAs fill whole waves of the GPU (one CTA per SM)
   // and short chunks still occupy every SM.  Cost model in key-tile periods:
   // waves * (tiles per split + overhead), the overhead standing for the
-  // prologue and, when split, the partial write and combine.
+  // prologue and, when split, the partial write; plus the combine: when the
+  // whole grid is one wave the splits of a row block share it (about one
+  // period), otherwise the last split reads every partial alone at one SM's
+  // L2 rate (about 0.6 period per split).
   const int heavy = n_retr_items * a.n_qtiles;  // grid slots (row-pair items leave half empty)
   int heavy_live = 0;
   for (int i = 0; i < n_retr_items; ++i)
@@ -989,7 +1094,9 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
       // if they fit, else as extra short waves
       const double spare = waves * sms - (double)heavy_live * sp;
       const double extra = light > spare ? std::ceil((light - spare) / sms) * light_tiles : 0.0;
-      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 3.0 : 1.0)) + extra;
+      const bool one_wave = (double)heavy * sp + light <= sms;
+      const double combine = sp > 1 ? (one_wave ? 1.0 : 0.6 * sp) : 0.0;
+      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 2.0 : 1.0)) + extra + combine;
       if (sp == 1 || cost < best * 0.97) {  // split only for a clear gain
         best = cost;
         n_split = sp;
@@ -998,14 +1105,18 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   }
   a.n_split = n_split;
   a.n_retr_items = n_retr_items;
+  // every CTA of a one-wave grid is resident at once (one CTA per SM, and the
+  // next kernel launches only after all of them have started)
+  a.coop = n_split > 1 && heavy * n_split + light <= sms ? 1 : 0;
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
   c->last_write_layer = layer;  // the kernel appends this call's rows to the layer's pages
   // Scratch: ticket counters -- one per (sequence, KV head) for the streaming
-  // units' ring append, then one per retrieval slot when split -- in a region
-  // of fixed capacity, so counters never land on an earlier call's partials;
-  // then the split partials.  Growing either part reallocates and zeroes it.
+  // units' ring append, then two per retrieval slot when split (arrivals and
+  // finished combines) -- in a region of fixed capacity, so counters never land
+  // on an earlier call's partials; then the split partials.  Growing either
+  // part reallocates and zeroes it.
   const int n_ring = cf.batch * cf.num_kv_heads;
-  const int need_cnt = n_ring + (n_split > 1 ? heavy : 0);
+  const int need_cnt = n_ring + (n_split > 1 ? 2 * heavy : 0);
   const int cnt_cap = std::max(need_cnt, c->prefill_cnt_cap);
   const size_t cnt_bytes = ((size_t)cnt_cap * sizeof(int) + 255) / 256 * 256;
   const size_t need = cnt_bytes + (n_split > 1 ? (size_t)heavy * n_split * 2 * kPartBytes : 0);
@@ -1028,6 +1139,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   }
   a.ring_counters = static_cast<int*>(c->prefill_ws);
   a.counters = a.ring_counters + n_ring;
+  a.done = a.counters + heavy;
   a.ws = n_split > 1 ? static_cast<uint8_t*>(c->prefill_ws) + cnt_bytes : nullptr;
   a.k_new = static_cast<const __nv_bfloat16*>(k_new);
   a.v_new = static_cast<const __nv_bfloat16*>(v_new);
