@@ -62,6 +62,7 @@ _SIGNATURES = {
     "aoh_attn_decode": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, C.c_size_t, _vp]),
     "aoh_attn_decode_noalloc": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "aoh_attn_prefill": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "aoh_attn_prefill_flash": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "aoh_kv_append": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp]),
     "aoh_classify_workspace_bytes": (C.c_size_t, [_i32, _i32, _i32, _i32]),
     "aoh_classify_eff_ranks": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,

@@ -13,7 +13,10 @@ q/k/v to the attention output, in ORIGINAL head order:
   after the last layer (:249-250).
 
 q_len == 1 runs the split-KV decode kernel; longer chunks run the prefill
-kernel.  Both are CUDA kernels in libaoh.so; there is no other path.
+kernel.  Both are CUDA kernels in libaoh.so; there is no other path.  A cache
+made with ``backend="flash"`` follows the reference's decoding-simulation
+protocol (attention_utils.py:45-89): its prompt goes in one call over the empty
+cache, every head attending causally to all of it, then decode steps as above.
 """
 from __future__ import annotations
 
@@ -60,10 +63,13 @@ def aoh_attention(cache: AoHKVCache, layer_idx: int, q: torch.Tensor, k: torch.T
                                C.c_void_p(ws.data_ptr()), ws.numel(), st)
         _lib.check(rc, "aoh_attn_decode")
     else:
-        rc = L.aoh_attn_prefill(cache._h, layer_idx, past, q_len, C.c_void_p(q.data_ptr()),
-                                C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
-                                C.c_void_p(out.data_ptr()), st)
-        _lib.check(rc, "aoh_attn_prefill")
+        # the decoding-simulation protocol prefills the prompt in one call with
+        # every head causal over it (attention_utils.py:45-89); a later
+        # multi-token call of that protocol raises NotImplementedError
+        fn = L.aoh_attn_prefill_flash if cache.backend == "flash" else L.aoh_attn_prefill
+        rc = fn(cache._h, layer_idx, past, q_len, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                C.c_void_p(v.data_ptr()), C.c_void_p(out.data_ptr()), st)
+        _lib.check(rc, "aoh_attn_prefill_flash" if cache.backend == "flash" else "aoh_attn_prefill")
     if advance and layer_idx == cache.num_layers - 1:
         cache.kv_seq_len += q_len
     return out

@@ -62,14 +62,22 @@ class AoHKVCache:
         owned: optional (num_layers, batch, num_kv_heads) mask of units stored
             on this device (multi-GPU partition); others get no pages.
         reserve_all: grant every retrieval page up front (no growth later).
+        backend: "eager" (the reference's eager protocol: streaming heads see
+            sink + window in every call) or "flash" (its decoding-simulation
+            protocol, eval/efficiency/attention_utils.py:45-89: the prompt is
+            prefilled in one call in which every head attends causally to the
+            whole prompt, then decode steps as in the eager protocol).
     """
 
     def __init__(self, labels, num_q_heads: int, *, batch: int = 1, sink_size: int = 128,
                  recent_size: int = 256, max_context: int, dtype: torch.dtype = torch.bfloat16,
                  device=None, num_pages: int | None = None, owned=None, reserve_all: bool = False,
-                 head_dim: int = HEAD_DIM):
+                 head_dim: int = HEAD_DIM, backend: str = "eager"):
         if sink_size < 0 or recent_size < 0:  # benchmark_llama31.py:257-258
             raise ValueError("sink_size and recent_size must be non-negative")
+        if backend not in ("eager", "flash"):
+            raise ValueError(f"backend must be 'eager' or 'flash', got {backend!r}")
+        self.backend = backend
         labels = np.asarray(labels, dtype=np.float64)
         if labels.ndim != 2:
             raise ValueError(f"labels must be (num_layers, num_kv_heads), got shape {labels.shape}")

@@ -73,6 +73,27 @@ int aoh_attn_prefill(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q
   return launch_append(c, layer, past_len, q_len, k_new, v_new, st);
 }
 
+int aoh_attn_prefill_flash(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q_len, const void* q,
+                           const void* k_new, const void* v_new, void* out, aoh_stream stream) {
+  int rc = check_common(c, layer, past_len, q_len, q, k_new, v_new, out, "aoh_attn_prefill_flash");
+  if (rc) return rc;
+  if (!q || !out) return fail(AOH_ERR_INVALID_ARGUMENT, "aoh_attn_prefill_flash: null q/out");
+  if (c->cfg.dtype != AOH_BF16)
+    return fail(AOH_ERR_UNSUPPORTED, "aoh_attn_prefill_flash: bf16 caches only (the protocol runs in half precision)");
+  if (past_len != 0)
+    return fail(AOH_ERR_UNSUPPORTED,
+                "aoh_attn_prefill_flash: the decoding-simulation protocol prefills the prompt in one call over an "
+                "empty cache (past_len is %d); decode steps use aoh_attn_decode",
+                past_len);
+  if (q_len == 0) return AOH_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // every head attends causally to the whole prompt; then every unit keeps
+  // what its label says (all rows, or the sink and the latest ring rows)
+  rc = launch_prefill_bf16(c, layer, 0, q_len, q, k_new, v_new, out, st, true);
+  if (rc) return rc;
+  return launch_append(c, layer, 0, q_len, k_new, v_new, st);
+}
+
 int aoh_kv_append(aoh_kv_cache* c, int32_t layer, int32_t past_len, int32_t q_len, const void* k_new,
                   const void* v_new, aoh_stream stream) {
   int rc = check_common(c, layer, past_len, q_len, nullptr, k_new, v_new, nullptr, "aoh_kv_append");

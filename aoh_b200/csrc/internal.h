@@ -131,8 +131,10 @@ size_t decode_workspace_bytes(const aoh_kv_cache* c);
 // Zero the tickets of the allocation-free decode scratch on `device` (if that
 // device has used it), stream-ordered; after a timed-out wait.
 int noalloc_clear_tickets(int device, cudaStream_t st);
+// all_causal: every head attends causally to the whole chunk (past_len must be
+// 0) and the kernel appends nothing -- the caller appends with launch_append.
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
-                        const void* v_new, void* out, cudaStream_t st);
+                        const void* v_new, void* out, cudaStream_t st, bool all_causal = false);
 int launch_attn_generic(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q,
                         const void* k_new, const void* v_new, void* out, cudaStream_t st);
 int launch_append(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* k_new,

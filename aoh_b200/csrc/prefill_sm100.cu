@@ -134,6 +134,11 @@ struct PrefillArgs {
   // the unit has read the ring.
   const __nv_bfloat16* k_new;  // (B, C, G, D)
   const __nv_bfloat16* v_new;
+  // 0: this kernel writes no rows to the pages (the caller appends them with
+  // another kernel); set for the one-shot prefill of the decoding-simulation
+  // protocol, where every item is listed as a retrieval item over an empty
+  // cache whatever its unit's label
+  int append;
   int* ring_counters;  // one per (sequence, KV head), zero between launches
   int n_items;
   // ((b * Hq + h0) << 3) | (row_pair << 2) | ((tiles - 1) << 1) | retrieval;
@@ -585,7 +590,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mma_commit(&bar_final);  // fires once every MMA issued above has completed (both O tiles final)
     }
     __syncwarp();
-  } else if (warp == kWarpAppend && ap_parts > 0) {
+  } else if (warp == kWarpAppend && ap_parts > 0 && a.append) {
     // ===================== append: retrieval rows =====================
     griddep_wait();  // this call's rows may be written by the previous kernel
     for (int blk = 0; blk < ap_blocks; ++blk) {
@@ -924,7 +929,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       }
     }
-    if (!retr) {
+    if (!retr && a.append) {
       // Streaming unit: this CTA's page reads are done (every tile it loaded
       // was consumed by an MMA before bar_final), so it takes the unit's
       // ticket; the last of the unit's CTAs writes the sink and ring rows.
@@ -1018,7 +1023,7 @@ int encode_pool_runs_map(aoh_kv_cache* c) {
 
 
 int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, const void* q, const void* k_new,
-                        const void* v_new, void* out, cudaStream_t st) {
+                        const void* v_new, void* out, cudaStream_t st, bool all_causal) {
   const auto& cf = c->cfg;
   if (!c->tmap_pool_runs_ok && cf.num_pages > 0) {
     int rc = encode_pool_runs_map(c);
@@ -1048,7 +1053,9 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
     for (int b = 0; b < cf.batch; ++b)
       for (int g = 0; g < cf.num_kv_heads; ++g) {
         if (!c->owned[c->unit(layer, b, g)]) continue;
-        const bool r = c->retrieval(layer, g);
+        // all_causal (one-shot prefill of the decoding-simulation protocol over
+        // an empty cache): every head attends causally to the whole chunk
+        const bool r = all_causal || c->retrieval(layer, g);
         if (r != (pass == 0)) continue;
         for (int j = 0; j < grp; j += 2) {  // pairs of query heads of the group
           if (a.n_items >= kMaxItemsP)
@@ -1108,6 +1115,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   // every CTA of a one-wave grid is resident at once (one CTA per SM, and the
   // next kernel launches only after all of them have started)
   a.coop = n_split > 1 && heavy * n_split + light <= sms ? 1 : 0;
+  a.append = all_causal ? 0 : 1;
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
   c->last_write_layer = layer;  // the kernel appends this call's rows to the layer's pages
   // Scratch: ticket counters -- one per (sequence, KV head) for the streaming

@@ -11,9 +11,10 @@ streaming heads over sink + window, then the append) and ``o_proj``.
 Differences kept on purpose: the library is label-driven, so the attention
 weights are not permuted into retrieval-first order (reorder_weights.py:19-60)
 and the output is already in original head order; ``make_cache`` takes the
-paged cache's sizing (batch, max_context, dtype, device) as keyword arguments
-and only the eager protocol exists (the reference's "flash" backend is a
-FlashAttention-2 decoding simulation with different semantics).
+paged cache's sizing (batch, max_context, dtype, device) as keyword arguments;
+``backend="flash"`` is the reference's decoding-simulation protocol
+(attention_utils.py:45-89) on this library's kernels, not on FlashAttention-2:
+the prompt in one forward with every head causal over it, then decode steps.
 
     make_cache, n_ret, n_str = patch_aoh_model(model, labels, 128, 256)
     cache = make_cache(max_context=65536)
@@ -123,7 +124,7 @@ def patch_aoh_model(model, labels: np.ndarray, sink_size: int, recent_size: int)
     ``(make_cache, n_ret, n_str)`` like the reference (benchmark_llama31.py:
     256-275).  ``make_cache(backend="eager", *, batch=1, max_context=None,
     dtype=None, device=None)`` builds the paged cache (default: the model's
-    max_position_embeddings, dtype and device)."""
+    max_position_embeddings, dtype and device); backend is "eager" or "flash"."""
     if sink_size < 0 or recent_size < 0:
         raise ValueError("sink_size and recent_size must be non-negative")
     cfg = model.config
@@ -146,12 +147,11 @@ def patch_aoh_model(model, labels: np.ndarray, sink_size: int, recent_size: int)
 
     def make_cache(backend: str = "eager", *, batch: int = 1, max_context: int | None = None, dtype=None,
                    device=None) -> AoHModelCache:
-        if backend != "eager":
-            raise NotImplementedError(f"backend {backend!r}: only the eager protocol is implemented")
         p = next(model.parameters())
         paged = AoHKVCache(labels, num_q, batch=batch, sink_size=sink_size, recent_size=recent_size,
                            max_context=int(max_context or cfg.max_position_embeddings),
-                           dtype=dtype or p.dtype, device=device or p.device, head_dim=head_dim)
+                           dtype=dtype or p.dtype, device=device or p.device, head_dim=head_dim,
+                           backend=backend)
         return AoHModelCache(paged)
 
     return make_cache, n_ret, n_str

@@ -210,6 +210,19 @@ AOH_API int aoh_attn_prefill(aoh_kv_cache* cache, int32_t layer, int32_t past_le
                      const void* q, const void* k_new, const void* v_new, void* out,
                      aoh_stream stream);
 
+/* The prefill of the decoding-simulation ("flash") protocol: replaces the
+ * prefill branch of aoh_flash_attention (eval/efficiency/attention_utils.py:
+ * 45-89, driven by flash_prefill in eval/results/run_longbench.py:119-139).
+ * The prompt goes in one call over an empty cache (past_len must be 0):
+ * every head -- streaming heads too -- attends causally to the whole prompt,
+ * then each unit keeps what its label says (retrieval: every row; streaming:
+ * the sink and the latest window rows, the reference's trim).  Decode steps of
+ * the protocol are aoh_attn_decode (the same arithmetic as the eager path for
+ * q_len = 1).  bf16 caches only; AOH_ERR_UNSUPPORTED for past_len != 0. */
+AOH_API int aoh_attn_prefill_flash(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,
+                                   const void* q, const void* k_new, const void* v_new, void* out,
+                                   aoh_stream stream);
+
 /* AoHKVCache.append_layer alone (benchmark_llama31.py:171-184): write q_len
  * new tokens at positions past_len.. into every unit of `layer`. */
 AOH_API int aoh_kv_append(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,

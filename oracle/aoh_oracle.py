@@ -158,6 +158,8 @@ class OracleKVCache:
     recent_size: int
     dtype: str = "f32"
     kv_seq_len: int = 0
+    # "eager" or "flash" (the decoding-simulation protocol, attention_utils.py:45-89)
+    backend: str = "eager"
     full_k: list = field(default_factory=list)
     full_v: list = field(default_factory=list)
     stream_k: list = field(default_factory=list)
@@ -202,6 +204,8 @@ def layer_attention(cache: OracleKVCache, layer_idx: int, q, k, v) -> np.ndarray
     B, C, Hq, D = q.shape
     G = k.shape[2]
     grp = Hq // G
+    if cache.backend == "flash":
+        return _layer_attention_flash(cache, layer_idx, q, k, v)
     kv_perm, q_perm = head_permutation(cache.labels[layer_idx], Hq, G)
     qh = np.ascontiguousarray(np.transpose(q, (0, 2, 1, 3))[:, q_perm])   # (B,Hq,C,D)
     kh = np.ascontiguousarray(np.transpose(k, (0, 2, 1, 3))[:, kv_perm])  # (B,G,C,D)
@@ -224,6 +228,58 @@ def layer_attention(cache: OracleKVCache, layer_idx: int, q, k, v) -> np.ndarray
             cached_len=0 if osk is None else osk.shape[2], sink_size=cache.sink_size,
             recent_size=cache.recent_size, dtype=cache.dtype))
     out_perm = np.concatenate(outs, axis=1) if len(outs) > 1 else outs[0]   # (B,Hq,C,D)
+    out = np.empty_like(out_perm)
+    out[:, q_perm] = out_perm
+    cache.append_layer(layer_idx, kh, vh)
+    if layer_idx == cache.num_layers - 1:
+        cache.kv_seq_len += C
+    return np.ascontiguousarray(np.transpose(out, (0, 2, 1, 3)))
+
+
+def _layer_attention_flash(cache: OracleKVCache, layer_idx: int, q, k, v) -> np.ndarray:
+    """The layer's attention under the decoding-simulation protocol;
+    eval/efficiency/attention_utils.py:45-89 (aoh_flash_attention, driven by
+    make_aoh_forward's flash branch, benchmark_llama31.py:212-215):
+
+    * the first call of a layer (its cache empty): every head, streaming heads
+      too, attends causally to the whole chunk (flash_attn_func causal over all
+      heads, :62-67);
+    * later calls: retrieval heads attend to their cached keys and the chunk,
+      streaming heads to their kept keys (sink + recent) and the chunk, both
+      causal with the queries aligned to the end of the keys (flash-attn's
+      causal convention when there are more keys than queries, :69-80) -- no
+      window mask;
+    * then the cache keeps every retrieval row and the sink and recent rows of
+      each streaming head (the in-place trim of :82-86 keeps exactly what
+      compress_stream keeps).
+
+    The arithmetic is the eager restatement's (fp32 scores and softmax,
+    probabilities rounded to the dtype); flash-attn's own rounding of the
+    unnormalised probabilities differs from it by at most a few ulps."""
+    B, C, Hq, D = q.shape
+    G = k.shape[2]
+    grp = Hq // G
+    kv_perm, q_perm = head_permutation(cache.labels[layer_idx], Hq, G)
+    qh = np.ascontiguousarray(np.transpose(q, (0, 2, 1, 3))[:, q_perm])
+    kh = np.ascontiguousarray(np.transpose(k, (0, 2, 1, 3))[:, kv_perm])
+    vh = np.ascontiguousarray(np.transpose(v, (0, 2, 1, 3))[:, kv_perm])
+    nr, ns = cache.n_ret[layer_idx], cache.n_str[layer_idx]
+    prefill = cache.full_k[layer_idx] is None and cache.stream_k[layer_idx] is None
+    if prefill:
+        out_perm = eager_attention(qh, repeat_kv(kh, grp), repeat_kv(vh, grp), 0, causal=True, dtype=cache.dtype)
+    else:
+        outs = []
+        if nr > 0:
+            fk = np.concatenate([cache.full_k[layer_idx], kh[:, :nr]], axis=2)
+            fv = np.concatenate([cache.full_v[layer_idx], vh[:, :nr]], axis=2)
+            outs.append(eager_attention(qh[:, : nr * grp], repeat_kv(fk, grp), repeat_kv(fv, grp),
+                                        fk.shape[2] - C, causal=True, dtype=cache.dtype))
+        if ns > 0:
+            sk = np.concatenate([cache.stream_k[layer_idx], kh[:, nr:]], axis=2)
+            sv = np.concatenate([cache.stream_v[layer_idx], vh[:, nr:]], axis=2)
+            outs.append(eager_attention(qh[:, nr * grp:], repeat_kv(sk, grp), repeat_kv(sv, grp),
+                                        sk.shape[2] - C, causal=True, dtype=cache.dtype))
+        out_perm = np.concatenate(outs, axis=1) if len(outs) > 1 else outs[0]
     out = np.empty_like(out_perm)
     out[:, q_perm] = out_perm
     cache.append_layer(layer_idx, kh, vh)

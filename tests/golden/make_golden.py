@@ -2,8 +2,11 @@
 
 Run in a container where the reference project (ernie-research/AoH) is
 available; pass its root with ``--ref`` (default: the REF_ROOT environment
-variable).  Writes ``tests/golden/*.npz``.  Nothing at test time imports the
-reference: the fixtures carry its outputs.
+variable) -- the project tree, or an installed copy of it.  Writes
+``tests/golden/*.npz`` (or ``--out``).  The decoding-simulation ("flash")
+cases run the reference's FlashAttention-2 path and need a CUDA device with
+flash_attn.  Nothing at test time imports the reference: the fixtures carry
+its outputs.
 
 Attention: the reference's patched attention forward
 (eval/efficiency/benchmark_llama31.py:187-253, make_aoh_forward) is driven with
@@ -31,6 +34,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
+OUT = HERE  # --out: where the fixtures go
 sys.path.insert(0, str(HERE.parents[1]))
 from aoh_b200 import synthetic as syn  # noqa: E402
 
@@ -59,6 +63,15 @@ ATTN_CASES = {
     "attn_f32_odd": dict(model="llama", dtype="f32", Hq=4, G=2, layers=1,
                          labels=[[0, 1]], sink=5, recent=23, chunks=[9, 30, 1, 17],
                          decode=4, seed=15, row_stride=1),
+    # the decoding-simulation protocol (backend "flash": FlashAttention-2 on a
+    # CUDA device): the prompt in one call, every head causal over it, the
+    # streaming heads trimmed, then decode steps
+    "attn_flash_bf16_small": dict(model="llama", dtype="bf16", Hq=8, G=2, layers=2,
+                                  labels=[[1, 0], [0, 1]], sink=16, recent=32, chunks=[300],
+                                  decode=6, seed=31, row_stride=7, backend="flash"),
+    "attn_flash_bf16_qwen25": dict(model="qwen", dtype="bf16", Hq=14, G=2, layers=1,
+                                   labels=[[0, 1]], sink=128, recent=256, chunks=[700],
+                                   decode=4, seed=32, row_stride=13, backend="flash"),
 }
 
 CLS_CASES = {
@@ -96,6 +109,8 @@ def case_inputs(spec, layer):
 
 def run_attention_case(name, spec, ref):
     L, Hq, G, D = spec["layers"], spec["Hq"], spec["G"], 128
+    backend = spec.get("backend", "eager")
+    dev = "cuda" if backend == "flash" else "cpu"  # flash_attn runs on a CUDA device only
     grp = Hq // G
     tdt = torch.float32 if spec["dtype"] == "f32" else torch.bfloat16
     labels = case_labels(spec, L, G)
@@ -109,7 +124,7 @@ def run_attention_case(name, spec, ref):
         q_perm = np.concatenate([np.arange(g * grp, (g + 1) * grp) for g in kv_perm])
         perms.append((kv_perm, q_perm))
         n_ret.append(len(rk)); n_str.append(len(sk))
-    cache = mod.AoHKVCache(L, n_ret, n_str, spec["sink"], spec["recent"])
+    cache = mod.AoHKVCache(L, n_ret, n_str, spec["sink"], spec["recent"], backend)
     inputs = [case_inputs(spec, l) for l in range(L)]
     steps = list(spec["chunks"]) + [1] * spec["decode"]
     total = sum(steps)
@@ -119,16 +134,16 @@ def run_attention_case(name, spec, ref):
         for l in range(L):
             q, k, v = (x[:, start:start + c] for x in inputs[l])
             kv_perm, q_perm = perms[l]
-            qt = torch.from_numpy(np.ascontiguousarray(q[:, :, q_perm])).to(tdt).reshape(1, c, Hq * D)
-            kt = torch.from_numpy(np.ascontiguousarray(k[:, :, kv_perm])).to(tdt).reshape(1, c, G * D)
-            vt = torch.from_numpy(np.ascontiguousarray(v[:, :, kv_perm])).to(tdt).reshape(1, c, G * D)
+            qt = torch.from_numpy(np.ascontiguousarray(q[:, :, q_perm])).to(dev).to(tdt).reshape(1, c, Hq * D)
+            kt = torch.from_numpy(np.ascontiguousarray(k[:, :, kv_perm])).to(dev).to(tdt).reshape(1, c, G * D)
+            vt = torch.from_numpy(np.ascontiguousarray(v[:, :, kv_perm])).to(dev).to(tdt).reshape(1, c, G * D)
             stub = types.SimpleNamespace(q_proj=lambda h, t=qt: t, k_proj=lambda h, t=kt: t,
                                          v_proj=lambda h, t=vt: t, o_proj=lambda x: x)
             fwd = mod.make_aoh_forward(l, n_ret[l], n_str[l], Hq, G, D)
             with torch.no_grad():
-                o, _ = fwd(stub, torch.zeros(1, c, 1, dtype=tdt), position_embeddings=None,
+                o, _ = fwd(stub, torch.zeros(1, c, 1, dtype=tdt, device=dev), position_embeddings=None,
                            past_key_values=cache)
-            o = o.float().numpy().reshape(c, Hq, D)
+            o = o.float().cpu().numpy().reshape(c, Hq, D)
             outs[l, start:start + c][:, q_perm] = o
         start += c
     # row subset: every row_stride-th prefill row of each chunk + all decode rows
@@ -148,7 +163,7 @@ def run_attention_case(name, spec, ref):
         out["out_bf16"] = syn.f32_to_bf16_bits(sel)
     else:
         out["out_f32"] = sel
-    np.savez_compressed(HERE / f"{name}.npz", **out)
+    np.savez_compressed(OUT / f"{name}.npz", **out)
     print(f"[golden] {name}: rows={len(rows)} out={sel.shape}", flush=True)
 
 
@@ -189,7 +204,7 @@ def run_classifier_case(name, spec, ref):
                 out[f"{mode}_{agg}_eff_ranks_kv"] = clf.eff_ranks_kv
                 out[f"{mode}_{agg}_sp{sp}_labels"] = labels
                 out[f"{mode}_classify_seconds"] = np.array(dt)
-    np.savez_compressed(HERE / f"{name}.npz", spec=np.array(repr(spec)), **out)
+    np.savez_compressed(OUT / f"{name}.npz", spec=np.array(repr(spec)), **out)
     print(f"[golden] {name} written", flush=True)
 
 
@@ -208,7 +223,7 @@ def run_kv_storage_cases(ref):
         full.append(ref["bench_llama"].kv_storage_gb_full(cfg, c["total"]))
         aoh.append(ref["bench_llama"].kv_storage_gb_aoh(cfg, n_ret, n_str, c["total"], 128, 256))
         spec.append(repr(c))
-    np.savez_compressed(HERE / "kv_storage.npz", names=np.array(names), specs=np.array(spec),
+    np.savez_compressed(OUT / "kv_storage.npz", names=np.array(names), specs=np.array(spec),
                         full_gb=np.array(full), aoh_gb=np.array(aoh))
     print(f"[golden] kv_storage: {len(names)} cases", flush=True)
 
@@ -228,7 +243,11 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("REF_ROOT", ""))
     ap.add_argument("--only", default="")
+    ap.add_argument("--out", default=str(HERE), help="directory for the .npz fixtures")
     args = ap.parse_args()
+    global OUT
+    OUT = Path(args.out)
+    OUT.mkdir(parents=True, exist_ok=True)
     if not args.ref:
         ap.error("pass --ref <reference project root> or set REF_ROOT")
     torch.set_num_threads(max(1, os.cpu_count() or 1))

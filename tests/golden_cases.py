@@ -15,6 +15,8 @@ from aoh_b200 import synthetic as syn
 GOLDEN = Path(__file__).resolve().parent / "golden"
 ATTN_CASES = ["attn_f32_window", "attn_f32_llama", "attn_bf16_qwen25", "attn_bf16_decode",
               "attn_f32_odd"]
+# the decoding-simulation protocol (backend "flash"); made on a CUDA device
+FLASH_CASES = ["attn_flash_bf16_small", "attn_flash_bf16_qwen25"]
 # bf16 outputs are compared at the bf16 tolerance, f32 outputs at the f32 one
 TOL = {"bf16": 2e-2, "f32": 1e-4}
 

@@ -16,7 +16,7 @@ def to_dev(x: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
 def make_cache(spec, labels, batch=1):
     total = sum(spec["chunks"]) + spec["decode"]
     return AoHKVCache(labels, spec["Hq"], batch=batch, sink_size=spec["sink"], recent_size=spec["recent"],
-                      max_context=total, dtype=DTYPES[spec["dtype"]])
+                      max_context=total, dtype=DTYPES[spec["dtype"]], backend=spec.get("backend", "eager"))
 
 
 def step(cache, layer, q, k, v):

@@ -64,6 +64,29 @@ def test_decode_from_empty_cache(cuda_device):
     assert errs["decode"] <= 2e-2
 
 
+@pytest.mark.parametrize("name", gc.FLASH_CASES)
+def test_flash_protocol_golden_cases(cuda_device, name):
+    """The decoding-simulation protocol (the prompt in one call, every head
+    causal over it, then decode steps) against the reference's FlashAttention-2
+    path on the same inputs."""
+    spec, got, ref, ck_ok = gc.replay(name, ge.make_cache, ge.step)
+    assert ck_ok
+    err = np.abs(got - ref).max()
+    assert err <= gc.TOL[spec["dtype"]], f"{name}: max abs err {err}"
+
+
+def test_flash_protocol_rejects_a_second_prompt_call(cuda_device):
+    labels = np.array([[1, 0]], dtype=np.float64)
+    cache = AoHKVCache(labels, 8, max_context=64, dtype=torch.bfloat16, backend="flash")
+    q = torch.zeros((1, 8, 8, 128), dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros((1, 8, 2, 128), dtype=torch.bfloat16, device="cuda")
+    aoh_attention(cache, 0, q, kv, kv)
+    with pytest.raises(NotImplementedError):
+        aoh_attention(cache, 0, q, kv, kv)  # a multi-token call over a non-empty cache
+    aoh_attention(cache, 0, q[:, :1], kv[:, :1], kv[:, :1])  # decode steps follow the prompt
+    assert cache.kv_seq_len == 9 and cache.device_status() == 0
+
+
 def _fill_cache_bf16(cache, layer, k_ctx, v_ctx, chunk=8192):
     """Write a context straight into the pages (AoHKVCache.append_layer)."""
     T = k_ctx.shape[1]

@@ -23,8 +23,8 @@ def test_patch_validates_arguments():
         patch_aoh_model(m, np.ones((3, 2)), -1, 256)
     make_cache, n_ret, n_str = patch_aoh_model(m, np.array([[1, 0], [0, 0], [1, 1]]), 128, 256)
     assert n_ret == [1, 0, 2] and n_str == [1, 2, 0]
-    with pytest.raises(NotImplementedError):
-        make_cache("flash")
+    with pytest.raises(ValueError):  # "eager" and "flash" are the reference's two protocols
+        make_cache("fused")
 
 
 def test_other_caches_use_the_original_forward():

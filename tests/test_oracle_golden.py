@@ -8,14 +8,15 @@ from aoh_b200 import synthetic as syn
 
 
 def _oracle_cache(spec, labels):
-    return orc.OracleKVCache(spec["layers"], labels, spec["sink"], spec["recent"], spec["dtype"])
+    return orc.OracleKVCache(spec["layers"], labels, spec["sink"], spec["recent"], spec["dtype"],
+                             backend=spec.get("backend", "eager"))
 
 
 def _oracle_step(cache, layer, q, k, v):
     return orc.layer_attention(cache, layer, q, k, v)
 
 
-@pytest.mark.parametrize("name", gc.ATTN_CASES)
+@pytest.mark.parametrize("name", gc.ATTN_CASES + gc.FLASH_CASES)
 def test_oracle_attention_matches_reference(name):
     spec, got, ref, ck_ok = gc.replay(name, _oracle_cache, _oracle_step)
     assert ck_ok, "seeded input generator drifted from the one the fixture was made with"
