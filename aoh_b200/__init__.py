@@ -7,7 +7,7 @@ head classifier, with the API of ernie-research/AoH.
 The CUDA kernels live in libaoh.so (built in-tree by ``python -m aoh_b200.build``)
 behind the C ABI of include/aoh.h.
 """
-from .attention import aoh_attention
+from .attention import aoh_attention, rope_qk
 from .cache import AoHKVCache, pages_needed
 from .classifier import AoHClassifier, compute_all_eff_ranks, compute_eff_rank, label_margins
 from .io import load_results, save_results
@@ -26,6 +26,7 @@ __all__ = [
     "AoHClassifier",
     "AoHKVCache",
     "aoh_attention",
+    "rope_qk",
     "compute_all_eff_ranks",
     "compute_eff_rank",
     "label_margins",

@@ -76,6 +76,8 @@ _SIGNATURES = {
     "aoh_kv_set_peers": (C.c_int, [_vp, _i32, _i32, C.POINTER(_vp), C.c_size_t, C.POINTER(_vp)]),
     "aoh_gather_wait": (C.c_int, [_vp, _i32, _i32, _vp]),
     "aoh_diag_exp2_poly": (C.c_int, [_vp, _vp, _i32, _vp]),
+    "aoh_rope_qk": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, C.c_float, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+                              _vp]),
 }
 IPC_HANDLE_BYTES = 64
 

@@ -73,3 +73,36 @@ def aoh_attention(cache: AoHKVCache, layer_idx: int, q: torch.Tensor, k: torch.T
     if advance and layer_idx == cache.num_layers - 1:
         cache.kv_seq_len += q_len
     return out
+
+
+def rope_qk(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+            q_norm_weight: torch.Tensor | None = None, k_norm_weight: torch.Tensor | None = None,
+            eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
+    """q_norm / k_norm (when weights are given) and the rotate-half RoPE of the
+    patched forward (benchmark_qwen.py:216-226) in one kernel.
+
+    q (B, C, Hq, D), k (B, C, G, D): bf16, contiguous (the projections'
+    views); cos / sin (B, C, D) bf16 from the model's rotary embedding.
+    Returns contiguous (q, k) ready for :func:`aoh_attention`."""
+    for name, t in (("q", q), ("k", k), ("cos", cos), ("sin", sin)):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError(f"{name} must be a contiguous bfloat16 CUDA tensor")
+    B, n, Hq, D = q.shape
+    G = k.shape[2]
+    if tuple(k.shape) != (B, n, G, D) or tuple(cos.shape) != (B, n, D) or tuple(sin.shape) != (B, n, D):
+        raise ValueError("q (B, C, Hq, D), k (B, C, G, D) and cos / sin (B, C, D) must agree")
+    if (q_norm_weight is None) != (k_norm_weight is None):
+        raise ValueError("give both norm weights or neither")
+    ws = []
+    for w in (q_norm_weight, k_norm_weight):
+        if w is not None:
+            w = w.to(torch.bfloat16).contiguous()
+            if tuple(w.shape) != (D,):
+                raise ValueError(f"norm weights must be ({D},)")
+        ws.append(w)
+    q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+    ptr = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    _lib.check(_lib.lib().aoh_rope_qk(ptr(q), ptr(k), ptr(cos), ptr(sin), ptr(ws[0]), ptr(ws[1]), float(eps), B, n,
+                                      Hq, G, D, ptr(q_out), ptr(k_out), C.c_void_p(_lib.stream_handle())),
+               "aoh_rope_qk")
+    return q_out, k_out

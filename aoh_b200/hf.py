@@ -3,9 +3,10 @@
 Counterpart of the reference's ``patch_aoh_model`` / ``make_aoh_forward``
 (eval/efficiency/benchmark_llama31.py:187-275, benchmark_qwen.py:196-292):
 every decoder layer's attention forward is replaced by one that projects
-q/k/v, applies Qwen3's QK-norm when the module has one (benchmark_qwen.py:
-216-220), applies the model's own rotary embedding, runs the head-mixed
-attention (``aoh_attention``: retrieval heads over every cached token,
+q/k/v, applies Qwen3's QK-norm when the module has one and the rotary
+embedding (benchmark_qwen.py:216-226) -- for bf16 caches in one kernel
+(``rope_qk``), otherwise with the model's own torch functions --, runs the
+head-mixed attention (``aoh_attention``: retrieval heads over every cached token,
 streaming heads over sink + window, then the append) and ``o_proj``.
 
 Differences kept on purpose: the library is label-driven, so the attention
@@ -28,7 +29,7 @@ import types
 import numpy as np
 import torch
 
-from .attention import aoh_attention
+from .attention import aoh_attention, rope_qk
 from .cache import AoHKVCache
 
 try:  # the Cache base class the model's forward expects (the reference subclasses it too)
@@ -96,21 +97,31 @@ def make_aoh_forward(layer_idx: int, num_q: int, num_kv: int, head_dim: int):
                                       attention_mask=attention_mask, past_key_values=past_key_values,
                                       cache_position=cache_position, **kwargs)
         bsz, q_len, _ = hidden_states.shape
-        q = self.q_proj(hidden_states).view(bsz, q_len, num_q, head_dim).transpose(1, 2)
-        k = self.k_proj(hidden_states).view(bsz, q_len, num_kv, head_dim).transpose(1, 2)
-        v = self.v_proj(hidden_states).view(bsz, q_len, num_kv, head_dim)
-        if hasattr(self, "q_norm"):
-            q = self.q_norm(q)
-        if hasattr(self, "k_norm"):
-            k = self.k_norm(k)
-        if position_embeddings is not None:
-            cos, sin = position_embeddings
-            rope = getattr(sys.modules[type(self).__module__], "apply_rotary_pos_emb")  # the model's own RoPE
-            q, k = rope(q, k, cos, sin)
         cache = past_key_values.paged
         dt = cache.dtype
-        q = q.transpose(1, 2).to(dt).contiguous()
-        k = k.transpose(1, 2).to(dt).contiguous()
+        q = self.q_proj(hidden_states).view(bsz, q_len, num_q, head_dim)
+        k = self.k_proj(hidden_states).view(bsz, q_len, num_kv, head_dim)
+        v = self.v_proj(hidden_states).view(bsz, q_len, num_kv, head_dim)
+        qn, kn = getattr(self, "q_norm", None), getattr(self, "k_norm", None)
+        if (position_embeddings is not None and dt == torch.bfloat16 and q.dtype == torch.bfloat16
+                and head_dim == 128):
+            # QK-norm (Qwen3) and RoPE in one kernel, straight into the layout the attention takes
+            cos, sin = position_embeddings
+            q, k = rope_qk(q.contiguous(), k.contiguous(), cos.to(torch.bfloat16).contiguous(),
+                           sin.to(torch.bfloat16).contiguous(), None if qn is None else qn.weight,
+                           None if kn is None else kn.weight, getattr(qn, "variance_epsilon", 1e-6))
+        else:
+            q, k = q.transpose(1, 2), k.transpose(1, 2)
+            if qn is not None:
+                q = qn(q)
+            if kn is not None:
+                k = kn(k)
+            if position_embeddings is not None:
+                cos, sin = position_embeddings
+                rope = getattr(sys.modules[type(self).__module__], "apply_rotary_pos_emb")  # the model's own RoPE
+                q, k = rope(q, k, cos, sin)
+            q = q.transpose(1, 2).to(dt).contiguous()
+            k = k.transpose(1, 2).to(dt).contiguous()
         v = v.to(dt).contiguous()
         out = aoh_attention(cache, layer_idx, q, k, v)  # attend, append, advance after the last layer
         out = out.reshape(bsz, q_len, num_q * head_dim).to(hidden_states.dtype)

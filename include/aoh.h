@@ -223,6 +223,21 @@ AOH_API int aoh_attn_prefill_flash(aoh_kv_cache* cache, int32_t layer, int32_t p
                                    const void* q, const void* k_new, const void* v_new, void* out,
                                    aoh_stream stream);
 
+/* Query/key preparation of the patched forward in one kernel: replaces the
+ * q_norm / k_norm (Qwen3's per-head RMSNorm) and apply_rotary_pos_emb steps
+ * of make_aoh_forward (eval/efficiency/benchmark_qwen.py:216-226,
+ * benchmark_llama31.py:204-209).  bf16 device tensors: q (batch, q_len,
+ * num_q_heads, 128), k (batch, q_len, num_kv_heads, 128) -- the projections'
+ * views --, cos / sin (batch, q_len, 128) as the model's rotary embedding
+ * returns them; q_norm_weight / k_norm_weight (128) or both NULL (no norm);
+ * eps the norms' epsilon.  Writes the rotated q_out / k_out (same shapes,
+ * contiguous, not aliasing the inputs): the attention entry points' q and
+ * k_new.  The rotation is bit-exact to the bf16 torch ops; a normed value may
+ * differ by one bf16 ulp (the mean square is summed in another order). */
+AOH_API int aoh_rope_qk(const void* q, const void* k, const void* cos, const void* sin, const void* q_norm_weight,
+                        const void* k_norm_weight, float eps, int32_t batch, int32_t q_len, int32_t num_q_heads,
+                        int32_t num_kv_heads, int32_t head_dim, void* q_out, void* k_out, aoh_stream stream);
+
 /* AoHKVCache.append_layer alone (benchmark_llama31.py:171-184): write q_len
  * new tokens at positions past_len.. into every unit of `layer`. */
 AOH_API int aoh_kv_append(aoh_kv_cache* cache, int32_t layer, int32_t past_len, int32_t q_len,

@@ -88,3 +88,42 @@ def test_mixed_labels_match_oracle(cuda_device, kind, monkeypatch):
     assert len(errs) == 2 * len(CHUNKS)
     assert max(errs) <= 2e-2, errs
     assert cache.paged.device_status() == 0
+
+
+@pytest.mark.parametrize("norm", [False, True])
+def test_rope_qk_matches_the_model_functions(cuda_device, norm):
+    """aoh_rope_qk against Qwen3's RMSNorm and apply_rotary_pos_emb run as
+    torch ops on the same bf16 inputs: RoPE alone bit for bit; with the norm,
+    every value within one bf16 ulp (the mean square is summed in another
+    order), nearly all of them equal."""
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
+
+    from aoh_b200 import rope_qk
+    B, C, Hq, G, D = 2, 37, 8, 2, 128
+    g = torch.Generator(device="cuda").manual_seed(12)
+    q = torch.randn((B, C, Hq, D), generator=g, device="cuda").to(torch.bfloat16)
+    k = (torch.randn((B, C, G, D), generator=g, device="cuda") * 3).to(torch.bfloat16)
+    pos = torch.arange(1000, 1000 + C, device="cuda").float()
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    emb = torch.cat([pos[:, None] * inv[None], pos[:, None] * inv[None]], dim=-1)
+    cos = emb.cos()[None].expand(B, C, D).to(torch.bfloat16).contiguous()
+    sin = emb.sin()[None].expand(B, C, D).to(torch.bfloat16).contiguous()
+    qn = kn = None
+    qt, kt = q.transpose(1, 2), k.transpose(1, 2)
+    if norm:
+        qn, kn = Qwen3RMSNorm(D, eps=1e-6).cuda().to(torch.bfloat16), Qwen3RMSNorm(D, eps=1e-6).cuda().to(torch.bfloat16)
+        with torch.no_grad():
+            qn.weight.copy_((1 + 0.1 * torch.randn(D, generator=g, device="cuda")).to(torch.bfloat16))
+            kn.weight.copy_((1 + 0.1 * torch.randn(D, generator=g, device="cuda")).to(torch.bfloat16))
+            qt, kt = qn(qt), kn(kt)
+    want_q, want_k = apply_rotary_pos_emb(qt, kt, cos, sin)
+    want_q, want_k = want_q.transpose(1, 2), want_k.transpose(1, 2)
+    got_q, got_k = rope_qk(q, k, cos, sin, None if qn is None else qn.weight, None if kn is None else kn.weight, 1e-6)
+    for got, want in ((got_q, want_q), (got_k, want_k)):
+        if not norm:
+            assert torch.equal(got, want)
+        else:
+            w = want.float()
+            ulp = torch.where(w == 0, torch.full_like(w, 2.0 ** -133), w.abs() * 2.0 ** -7)
+            assert bool(((got.float() - w).abs() <= ulp).all())
+            assert (got == want).float().mean().item() > 0.99
