@@ -27,15 +27,18 @@
 //     O^T += V^T P^T (ldmatrix.trans).  Query rows >= GRP are zero padding.
 //   merge: the 4 warps' (O, m, l) are merged in shared memory.  A unit with one
 //     CTA writes its output directly.  A unit with several CTAs is split in
-//     multiples of 8, launched as thread-block clusters of 8: the 8 CTAs of a
-//     cluster merge their partials through distributed shared memory (each
-//     CTA reduces 1/8 of the outputs), one partial per cluster goes to the
-//     workspace, and the last cluster of the unit to finish (atomic ticket --
-//     nothing waits on another cluster) combines the unit's partials with the
-//     log-sum-exp rule, again spread over its 8 CTAs.  The finishing CTA then
-//     writes the new token's K/V into its page slot (attend, then append).
-//     The ticket is an acq_rel atomic after a cluster barrier: cumulative over
-//     the cluster's partial stores, no per-thread fences.
+//     multiples of the cluster size C (8, or 4 for layers whose rounding to
+//     8 would leave too few CTAs streaming -- chosen per launch), launched as
+//     thread-block clusters of C: the C CTAs of a cluster merge their partials
+//     through distributed shared memory (each CTA reduces 1/C of the outputs),
+//     one partial per cluster goes to the workspace, and per cluster slice the
+//     last cluster of the unit to store it (atomic ticket -- nothing waits on
+//     another cluster) combines the unit's partials with the log-sum-exp rule.
+//     The ticket is an acq_rel atomic after __syncthreads: cumulative over the
+//     CTA's slice stores, no per-thread fences.  A retrieval unit's new token
+//     is written into its page slot right after the dependency wait (no CTA
+//     of the launch attends to it); a streaming unit's after every read of
+//     the unit (attend, then append).
 //   output gather (multi-GPU, when peers are attached): the CTA that finishes
 //     a unit stores its rows into every rank's output region (peer pointers)
 //     and, after a barrier, publishes a per-(layer, unit) flag to every rank
@@ -69,13 +72,22 @@ constexpr int kOPitch = kHeadDim + 4;  // padded row of the warp-merge scratch
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
 // Workspace tickets: per (unit, cluster slice) one ticket, then per unit one
 // count of stored slices (multi-GPU publish); all zero between launches.
-constexpr int kCounterBytes = kMaxUnits * (8 + 1) * 4;
-constexpr int kCluster = 8;
-static_assert(kMaxGrp * kHeadDim / kCluster <= kThreads, "a cluster CTA's output slice is one element per thread");
+// Split units run in thread-block clusters of 8 CTAs, or of 4 when clusters of
+// 8 would leave the GPU short of streaming CTAs (see plan_and_launch).
+constexpr int kClusterBig = 8, kClusterSmall = 4;
+constexpr int kCounterBytes = kMaxUnits * (kClusterBig + 1) * 4;  // holds either layout
+constexpr int kMaxPartials = kMaxCtas / kClusterSmall;
+// A cluster CTA's output slice spans at most three rows of head_dim outputs.
+static_assert(kMaxGrp * kHeadDim / kClusterSmall <= 2 * kHeadDim, "slice rows staged in shared memory");
+// Consumer warp w takes pages w, w + 4, ...: with a whole number of stages per
+// warp every stage belongs to one warp, which waits on its phases in order (a
+// stage shared by two warps could be waited on two phases ahead, which a
+// parity wait cannot tell from the phase before).
+static_assert(kStages % kConsumerWarps == 0, "each ring stage must belong to a single consumer warp");
 
 struct DecodePlan {
   int n_units;
-  int total_ctas;                // CTAs with work; the grid is padded to a multiple of kCluster
+  int total_ctas;                // CTAs with work; the grid is padded to a multiple of the cluster size
   int unit[kMaxUnits];           // ((b * G + g) << 1) | is_retrieval
   int cta_begin[kMaxUnits + 1];  // prefix sum of splits; units with > 1 split are cluster-aligned
 };
@@ -90,7 +102,7 @@ struct DecodeArgs {
   int T;             // past_len: cached positions are [0, T), the query is at T
   const int* T_dev;  // if non-null, past_len is read from here (CUDA-graph replay)
   float scale_log2;  // D^-0.5 * log2(e)
-  float* ws;         // per-cluster partials, (kMaxCtas / kCluster) x kPartialFloats
+  float* ws;         // per-cluster partials, kMaxPartials x kPartialFloats
   int* counters;     // [unit][slice] tickets, then [unit] stored-slice counts; zero between launches
   // 0: the kernel before this one in the stream wrote this layer's pages
   // (e.g. a prefill chunk's append), so no page is streamed before waiting
@@ -214,7 +226,10 @@ __device__ __forceinline__ void append_token(const DecodeArgs& a, const UnitView
   *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(src)[c8];
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// kCluster: 8 or 4.  Both instances hold 3 CTAs per SM (shared memory); the
+// 4-CTA instance needs the register bound to stay within 128 registers.
+template <int kCluster>
+__global__ void __launch_bounds__(kThreads, kCluster == kClusterBig ? 1 : 3)
     decode_bf16_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodePlan plan) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -623,44 +638,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       return;
     }
     // ============ the last cluster to store slice `rank` combines it over the unit's nk partials ============
-    // This thread's element of up to 32 partials is loaded with the slice rows'
-    // m and l, in one round of loads; more partials are read as they are used.
-    const int e_mine = e_lo + tid;  // a CTA's slice is at most kThreads elements: one per thread
-    const bool mine = e_mine < e_hi;
-    constexpr int kPre = 32;
-    float v[kPre];
-#pragma unroll
-    for (int j = 0; j < kPre; ++j)
-      v[j] = (mine && j < nk) ? __ldcg(parts + e_mine + (size_t)j * kPartialFloats) : 0.f;
-    const int q_lo = e_lo >> 7, n_rows = ((e_hi - 1) >> 7) - q_lo + 1;  // the slice spans one or two rows
+    const int q_lo = e_lo >> 7, n_rows = ((e_hi - 1) >> 7) - q_lo + 1;  // the slice spans up to three rows
     float* sml = reinterpret_cast<float*>(smem);                         // [row][k][m, l] (the ring is free)
-    for (int i = tid; i < nk * n_rows; i += kThreads) {
-      const int r = i / nk, k = i % nk;
-      const float* pm = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + q_lo + r;
-      sml[(r * (kMaxSplit / kCluster) + k) * 2] = __ldcg(pm);
-      sml[(r * (kMaxSplit / kCluster) + k) * 2 + 1] = __ldcg(pm + kMaxGrp);
-    }
-    __syncthreads();
-    if (mine) {
-      const float* ml = sml + ((e_mine >> 7) - q_lo) * (kMaxSplit / kCluster) * 2;
-      float M = -INFINITY;
-      for (int k = 0; k < nk; ++k) M = fmaxf(M, ml[2 * k]);
-      const float Mu = M == -INFINITY ? 0.f : M;
-      float acc = 0.f, L = 0.f;
+    constexpr int kPre = kCluster >= 8 ? 32 : 64;  // partials prefetched per element (the unit has nk)
+    if (e_hi - e_lo <= kThreads) {
+      // This thread's element of up to kPre partials is loaded with the slice
+      // rows' m and l, in one round of loads; more partials are read as they are used.
+      const int e_mine = e_lo + tid;
+      const bool mine = e_mine < e_hi;
+      float v[kPre];
 #pragma unroll
-      for (int j = 0; j < kPre; ++j) {
-        if (j < nk) {
-          const float f = fast_exp2(ml[2 * j] - Mu);
-          acc += v[j] * f;
-          L += ml[2 * j + 1] * f;
+      for (int j = 0; j < kPre; ++j)
+        v[j] = (mine && j < nk) ? __ldcg(parts + e_mine + (size_t)j * kPartialFloats) : 0.f;
+      for (int i = tid; i < nk * n_rows; i += kThreads) {
+        const int r = i / nk, k = i % nk;
+        const float* pm = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + q_lo + r;
+        sml[(r * (kMaxSplit / kCluster) + k) * 2] = __ldcg(pm);
+        sml[(r * (kMaxSplit / kCluster) + k) * 2 + 1] = __ldcg(pm + kMaxGrp);
+      }
+      __syncthreads();
+      if (mine) {
+        const float* ml = sml + ((e_mine >> 7) - q_lo) * (kMaxSplit / kCluster) * 2;
+        float M = -INFINITY;
+        for (int k = 0; k < nk; ++k) M = fmaxf(M, ml[2 * k]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float acc = 0.f, L = 0.f;
+#pragma unroll
+        for (int j = 0; j < kPre; ++j) {
+          if (j < nk) {
+            const float f = fast_exp2(ml[2 * j] - Mu);
+            acc += v[j] * f;
+            L += ml[2 * j + 1] * f;
+          }
         }
+        for (int k = kPre; k < nk; ++k) {
+          const float f = fast_exp2(ml[2 * k] - Mu);
+          acc += __ldcg(parts + e_mine + (size_t)k * kPartialFloats) * f;
+          L += ml[2 * k + 1] * f;
+        }
+        s_out[tid] = __float2bfloat16(acc / L);
       }
-      for (int k = kPre; k < nk; ++k) {
-        const float f = fast_exp2(ml[2 * k] - Mu);
-        acc += __ldcg(parts + e_mine + (size_t)k * kPartialFloats) * f;
-        L += ml[2 * k + 1] * f;
+    } else {
+      // a slice longer than the CTA (small clusters, large query groups): the
+      // rows' m and l first, then each element's partials as they are used
+      for (int i = tid; i < nk * n_rows; i += kThreads) {
+        const int r = i / nk, k = i % nk;
+        const float* pm = parts + (size_t)k * kPartialFloats + kMaxGrp * kHeadDim + q_lo + r;
+        sml[(r * (kMaxSplit / kCluster) + k) * 2] = __ldcg(pm);
+        sml[(r * (kMaxSplit / kCluster) + k) * 2 + 1] = __ldcg(pm + kMaxGrp);
       }
-      s_out[tid] = __float2bfloat16(acc / L);
+      __syncthreads();
+      for (int e = e_lo + tid; e < e_hi; e += kThreads) {
+        const float* ml = sml + ((e >> 7) - q_lo) * (kMaxSplit / kCluster) * 2;
+        float M = -INFINITY;
+        for (int k = 0; k < nk; ++k) M = fmaxf(M, ml[2 * k]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float acc = 0.f, L = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < nk; ++k) {
+          const float f = fast_exp2(ml[2 * k] - Mu);
+          acc += __ldcg(parts + e + (size_t)k * kPartialFloats) * f;
+          L += ml[2 * k + 1] * f;
+        }
+        s_out[e - e_lo] = __float2bfloat16(acc / L);
+      }
     }
     __syncthreads();
     // the slice (grp * 16 elements, starting at a multiple of 8) leaves as 16-byte stores
@@ -694,22 +735,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!retr && tid < 32) append_token(a, uv, bt, b, g, lane);
 }
 
-// CTAs resident at once when launched in clusters of kCluster, per device
-// (filled once per device under g_attrs' lock, read-only afterwards)
-int g_max_ctas[kMaxDevices] = {};
+// Per device: the SM count and the CTAs resident at once when launched in
+// clusters of 8 ([0]) and of 4 ([1]) (filled once per device under g_attrs'
+// lock, read-only afterwards).
+int g_sms[kMaxDevices] = {};
+int g_max_ctas[kMaxDevices][2] = {};
 PerDeviceOnce g_attrs;
 
 // attr must have room for 2 attributes: cluster shape and programmatic
 // stream serialization (the kernel may start while the previous kernel in the
 // stream finishes; it synchronises with griddepcontrol.wait).
-cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, bool pdl) {
+cudaLaunchConfig_t launch_config(int grid, int cluster, cudaStream_t st, cudaLaunchAttribute* attr, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kDynSmem;
   cfg.stream = st;
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.x = cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -719,55 +762,87 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
   return cfg;
 }
 
-// Kernel attributes and the resident-CTA count of `device` (the current one).
-int ensure_kernel_attrs(int device, int* max_ctas) {
-  const int rc = g_attrs.run(device, [device] {
-    int r = cuda_check(cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kDynSmem),
-                       "decode: set smem attribute");
-    if (r) return r;
-    cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = launch_config(kCluster, nullptr, attr, false);
-    int clusters = 0;
-    r = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel, &cfg), "decode: cluster occupancy");
-    if (r) return r;
-    if (clusters <= 0) return fail(AOH_ERR_CUDA, "decode kernel clusters cannot be resident");
-    g_max_ctas[device] = std::min(kMaxCtas, clusters * kCluster);
-    return (int)AOH_OK;
-  });
-  if (rc) return rc;
-  *max_ctas = g_max_ctas[device];
+template <int kCl>
+int cluster_capacity(int* ctas) {
+  int r = cuda_check(cudaFuncSetAttribute(decode_bf16_kernel<kCl>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kDynSmem),
+                     "decode: set smem attribute");
+  if (r) return r;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config(kCl, kCl, nullptr, attr, false);
+  int clusters = 0;
+  r = cuda_check(cudaOccupancyMaxActiveClusters(&clusters, decode_bf16_kernel<kCl>, &cfg), "decode: cluster occupancy");
+  if (r) return r;
+  if (clusters <= 0) return fail(AOH_ERR_CUDA, "decode kernel clusters cannot be resident");
+  *ctas = std::min(kMaxCtas, clusters * kCl);
   return AOH_OK;
+}
+
+// Kernel attributes, SM count and resident-CTA counts of `device` (the current one).
+int ensure_kernel_attrs(int device) {
+  return g_attrs.run(device, [device] {
+    int r = cuda_check(cudaDeviceGetAttribute(&g_sms[device], cudaDevAttrMultiProcessorCount, device),
+                       "decode: SM count");
+    if (r) return r;
+    r = cluster_capacity<kClusterBig>(&g_max_ctas[device][0]);
+    if (r) return r;
+    return cluster_capacity<kClusterSmall>(&g_max_ctas[device][1]);
+  });
 }
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 // Splits of a unit with `pages` units of work at `per` pages per CTA: 1, or a
 // multiple of the cluster size.
-int splits_for(int64_t pages, int64_t per) {
+int splits_for(int64_t pages, int64_t per, int cluster) {
   const int64_t n = std::max<int64_t>(1, (pages + per - 1) / per);
   if (n == 1) return 1;
-  return (int)std::min<int64_t>(kMaxSplit, round_up((int)std::min<int64_t>(n, kMaxSplit), kCluster));
+  return (int)std::min<int64_t>(kMaxSplit, round_up((int)std::min<int64_t>(n, kMaxSplit), cluster));
+}
+
+// The smallest pages-per-CTA whose grid fits `target` CTAs; the grid it gives
+// and its CTAs of the units with the most splits (the ones that stream the
+// longest).
+struct SplitPlan {
+  int64_t per;
+  int grid, long_ctas;
+};
+SplitPlan plan_splits(const int64_t* pages, int n, int64_t total, int target, int cluster) {
+  SplitPlan sp;
+  sp.per = std::max<int64_t>(4, (total + target - 1) / target);
+  for (;;) {
+    int ctas = 0, most = 0, n_most = 0;
+    for (int i = 0; i < n; ++i) {
+      const int k = splits_for(pages[i], sp.per, cluster);
+      ctas += k;
+      if (k > most) most = k, n_most = 0;
+      if (k == most) ++n_most;
+    }
+    sp.grid = round_up(ctas, cluster);
+    sp.long_ctas = most * n_most;
+    if (sp.grid <= target || sp.per > total) break;
+    sp.per = sp.per + sp.per / 16 + 1;
+  }
+  return sp;
 }
 
 }  // namespace
 
-// Workspace: one ticket per unit of a launch, then one partial (O, m, l) per
-// cluster -- at most kMaxCtas / kCluster of them.
+// Workspace: tickets, then one partial (O, m, l) per cluster -- at most
+// kMaxPartials of them.
 size_t decode_workspace_bytes(const aoh_kv_cache*) {
-  return (size_t)kCounterBytes + (size_t)(kMaxCtas / kCluster) * kPartialFloats * sizeof(float);
+  return (size_t)kCounterBytes + (size_t)kMaxPartials * kPartialFloats * sizeof(float);
 }
 
-// Plan the layer's split over at most `max_clusters` cluster partials and launch.
+// Plan the layer's split over at most `max_partials` cluster partials and launch.
 static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
-                    const void* v_new, void* out, void* ws, int max_clusters, cudaStream_t st,
-                    const int* past_len_dev) {
+                           const void* v_new, void* out, void* ws, int max_partials, cudaStream_t st,
+                           const int* past_len_dev) {
   const auto& cf = c->cfg;
   const int grp = cf.num_q_heads / cf.num_kv_heads;
   if (grp > kMaxGrp)
     return fail(AOH_ERR_UNSUPPORTED, "decode: query heads per KV head (%d) above %d", grp, kMaxGrp);
-  int max_ctas = 0;
-  int rc = ensure_kernel_attrs(c->device, &max_ctas);
+  int rc = ensure_kernel_attrs(c->device);
   if (rc) return rc;
 
   // ---- plan: the units of this layer stored here, split so one wave fills the GPU ----
@@ -792,31 +867,41 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
       ++n;
     }
   if (n == 0) return AOH_OK;
-  const int target = std::min(max_ctas, max_clusters * kCluster);
-  int64_t per = std::max<int64_t>(4, (total + target - 1) / target);
-  int grid = 0;
-  for (;;) {
-    int ctas = 0;
-    for (int i = 0; i < n; ++i) ctas += splits_for(pages[i], per);
-    grid = round_up(ctas, kCluster);
-    if (grid <= target || per > total) break;
-    per = per + per / 16 + 1;
+  // Clusters of 8 keep the merge tail short.  But every split unit is rounded
+  // to a multiple of the cluster size, and with many units (a batch) that can
+  // leave the CTAs that stream the longest below ~2.25 per SM, where the layer
+  // stops being bound by HBM (measured: 1.73 per SM streamed at 0.89 of the
+  // copy peak, 2.16 per SM in clusters of 4 at 0.99-1.07).  Then clusters of 4,
+  // whose finer rounding (and denser packing) keeps more CTAs streaming, are
+  // worth their longer merge.
+  int cluster = kClusterBig;
+  SplitPlan sp = plan_splits(pages, n, total, std::min(g_max_ctas[c->device][0], max_partials * kClusterBig),
+                             kClusterBig);
+  if (4 * sp.long_ctas < 9 * g_sms[c->device]) {
+    const SplitPlan s4 = plan_splits(pages, n, total,
+                                     std::min(g_max_ctas[c->device][1], max_partials * kClusterSmall), kClusterSmall);
+    if (s4.long_ctas > sp.long_ctas) {
+      sp = s4;
+      cluster = kClusterSmall;
+    }
   }
+  const int64_t per = sp.per;
+  const int grid = sp.grid;
   if (grid > kMaxCtas) return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d CTAs", grid);
-  if (grid / kCluster > max_clusters)
+  if (grid / cluster > max_partials)
     return fail(AOH_ERR_UNSUPPORTED, "decode: plan needs %d cluster partials, the workspace holds %d",
-                grid / kCluster, max_clusters);
+                grid / cluster, max_partials);
   // units split across clusters first (cluster-aligned), single-CTA units after
   DecodePlan plan;
   plan.n_units = n;
   int k = 0, begin = 0;
   for (int pass = 0; pass < 2; ++pass)
     for (int i = 0; i < n; ++i) {
-      const int sp = splits_for(pages[i], per);
-      if ((sp > 1) != (pass == 0)) continue;
+      const int spl = splits_for(pages[i], per, cluster);
+      if ((spl > 1) != (pass == 0)) continue;
       plan.unit[k] = code[i];
       plan.cta_begin[k] = begin;
-      begin += sp;
+      begin += spl;
       ++k;
     }
   plan.cta_begin[n] = begin;
@@ -853,10 +938,12 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
     }
   }
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = launch_config(grid, st, attr, true);
+  cudaLaunchConfig_t cfg = launch_config(grid, cluster, st, attr, true);
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
   c->last_write_layer = layer;  // the kernel appends the new token to this layer
-  return cuda_check(cudaLaunchKernelEx(&cfg, decode_bf16_kernel, a, plan), "decode kernel launch");
+  return cuda_check(cluster == kClusterBig ? cudaLaunchKernelEx(&cfg, decode_bf16_kernel<kClusterBig>, a, plan)
+                                           : cudaLaunchKernelEx(&cfg, decode_bf16_kernel<kClusterSmall>, a, plan),
+                    "decode kernel launch");
 }
 
 int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, const void* k_new,
@@ -867,7 +954,7 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
                 decode_workspace_bytes(c));
   if (reinterpret_cast<uintptr_t>(ws) % 16)
     return fail(AOH_ERR_INVALID_ARGUMENT, "decode: workspace must be 16-byte aligned");
-  return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, ws, kMaxCtas / kCluster, st, past_len_dev);
+  return plan_and_launch(c, layer, past_len, q, k_new, v_new, out, ws, kMaxPartials, st, past_len_dev);
 }
 
 // ---------------------------------------------------------------------------
@@ -875,14 +962,14 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
 //
 // For callers that cannot allocate device memory (see include/aoh.h), the
 // decode workspace lives in a file-scope device array instead of a
-// caller-provided buffer.  It holds the per-unit tickets and up to
-// kNoAllocClusters cluster partials: 9 KB + 64 x 4160 B = 275,456 bytes, which
-// every GPU that loads this library keeps until the process exits.  The array
-// is shared by every call: calls that overlap on the GPU race on it.
+// caller-provided buffer.  It holds the tickets and up to kNoAllocPartials
+// cluster partials: 9 KB + 64 x 4160 B = 275,456 bytes, which every GPU that
+// loads this library keeps until the process exits.  The array is shared by
+// every call: calls that overlap on the GPU race on it.
 // ---------------------------------------------------------------------------
-constexpr int kNoAllocClusters = 64;
+constexpr int kNoAllocPartials = 64;
 constexpr size_t kNoAllocScratchBytes =
-    (size_t)kCounterBytes + (size_t)kNoAllocClusters * kPartialFloats * sizeof(float);
+    (size_t)kCounterBytes + (size_t)kNoAllocPartials * kPartialFloats * sizeof(float);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
@@ -947,9 +1034,9 @@ extern "C" int aoh_attn_decode_noalloc(aoh_kv_cache* c, int32_t layer, int32_t p
   void* scratch = nullptr;
   rc = noalloc_scratch(dev, st, &scratch);
   if (rc) return rc;
-  // The plan never needs more than kNoAllocClusters partials: its grid is at
-  // most max(resident CTAs, kMaxUnits rounded to clusters) = 256 CTAs = 32
-  // clusters; plan_and_launch would reject a larger one.
-  return plan_and_launch(c, layer, plan_len, q, k_new, v_new, out, scratch, kNoAllocClusters, st,
+  // The plan's targets are capped at kNoAllocPartials partials (512 CTAs in
+  // clusters of 8, 256 in clusters of 4); plan_and_launch rejects a grid that
+  // needs more (more units than that).
+  return plan_and_launch(c, layer, plan_len, q, k_new, v_new, out, scratch, kNoAllocPartials, st,
                          dev_len ? c->dev_err + 1 : nullptr);
 }

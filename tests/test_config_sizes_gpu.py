@@ -123,3 +123,33 @@ def test_config4_batch8_256k_skewed_decode(cuda_device):
             worst = max(worst, float(np.abs(got[b, 0, g * grp:(g + 1) * grp] - want).max()))
     assert worst <= 2e-2, worst
     assert cache.kv_seq_len == T + 1
+
+
+def test_decode_group7_batch8_clusters_of_4(cuda_device):
+    """Qwen2.5-7B heads (28 / 4, group 7), batch 8, every KV head retrieval,
+    16,384 cached tokens: 32 split units, which the plan runs in clusters of 4
+    (clusters of 8 would leave fewer than 2.25 streaming CTAs per SM).  A
+    cluster CTA's output slice (7 x 128 / 4 = 224 outputs) is longer than the
+    CTA, so its threads combine two outputs each.  Every unit against the oracle."""
+    Hq, G, B, D, T, sink, recent = 28, 4, 8, 128, 16384, 128, 256
+    grp = Hq // G
+    labels = np.ones((1, G), dtype=np.float64)
+    cache = AoHKVCache(labels, Hq, batch=B, sink_size=sink, recent_size=recent, max_context=T + 1,
+                       dtype=torch.bfloat16, reserve_all=True)
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    k = (torch.randn((B, T, G, D), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, T, G, D), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    _fill(cache, 0, k, v, T)
+    q = torch.randn((B, 1, Hq, D), generator=gen, device="cuda").to(torch.bfloat16)
+    kn = (torch.randn((B, 1, G, D), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    vn = (torch.randn((B, 1, G, D), generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    got = F(aoh_attention(cache, 0, q, kn, vn))
+    assert cache.device_status() == 0
+    qn, knn, vnn, kc, vc = F(q), F(kn), F(vn), F(k), F(v)
+    worst = 0.0
+    for b in range(B):
+        for g in range(G):
+            want = orc.decode_unit(qn[b, 0, g * grp:(g + 1) * grp], knn[b, 0, g], vnn[b, 0, g], kc[b, :, g],
+                                   vc[b, :, g], True, T, sink, recent, "bf16")
+            worst = max(worst, float(np.abs(got[b, 0, g * grp:(g + 1) * grp] - want).max()))
+    assert worst <= 2e-2, worst
