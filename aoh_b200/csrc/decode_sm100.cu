@@ -70,12 +70,13 @@ constexpr int kMaxSplit = 1024;
 constexpr int kPartialFloats = kMaxGrp * kHeadDim + 2 * kMaxGrp;
 constexpr int kOPitch = kHeadDim + 4;  // padded row of the warp-merge scratch
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
-// Workspace tickets: per (unit, cluster slice) one ticket, then per unit one
-// count of stored slices (multi-GPU publish); all zero between launches.
 // Split units run in thread-block clusters of 8 CTAs, or of 4 when clusters of
 // 8 would leave the GPU short of streaming CTAs (see plan_and_launch).
 constexpr int kClusterBig = 8, kClusterSmall = 4;
-constexpr int kCounterBytes = kMaxUnits * (kClusterBig + 1) * 4;  // holds either layout
+// Workspace tickets: per (unit, cluster slice) one ticket, then per unit one
+// count of stored slices (multi-GPU publish); all zero between launches.  Sized
+// for clusters of 8, so it holds either layout.
+constexpr int kCounterBytes = kMaxUnits * (kClusterBig + 1) * 4;
 constexpr int kMaxPartials = kMaxCtas / kClusterSmall;
 // A cluster CTA's output slice spans at most three rows of head_dim outputs.
 static_assert(kMaxGrp * kHeadDim / kClusterSmall <= 2 * kHeadDim, "slice rows staged in shared memory");
@@ -869,15 +870,17 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   if (n == 0) return AOH_OK;
   // Clusters of 8 keep the merge tail short.  But every split unit is rounded
   // to a multiple of the cluster size, and with many units (a batch) that can
-  // leave the CTAs that stream the longest below ~2.25 per SM, where the layer
-  // stops being bound by HBM (measured: 1.73 per SM streamed at 0.89 of the
-  // copy peak, 2.16 per SM in clusters of 4 at 0.99-1.07).  Then clusters of 4,
-  // whose finer rounding (and denser packing) keeps more CTAs streaming, are
-  // worth their longer merge.
+  // leave the CTAs that stream the longest below 2 per SM, where the layer
+  // stops being bound by HBM.  Then clusters of 4, whose finer rounding (and
+  // denser packing) keeps more CTAs streaming, are worth their longer merge.
+  // Measured on batch-8 256K layers: 256 long CTAs (1.73 per SM) in clusters
+  // of 8 streamed at 0.89 of the copy peak, 320 in clusters of 4 at 0.99; with
+  // 320 long CTAs in clusters of 8 (2.16 per SM, half the batch per GPU),
+  // clusters of 4 were 5% slower.
   int cluster = kClusterBig;
   SplitPlan sp = plan_splits(pages, n, total, std::min(g_max_ctas[c->device][0], max_partials * kClusterBig),
                              kClusterBig);
-  if (4 * sp.long_ctas < 9 * g_sms[c->device]) {
+  if (sp.long_ctas < 2 * g_sms[c->device]) {
     const SplitPlan s4 = plan_splits(pages, n, total,
                                      std::min(g_max_ctas[c->device][1], max_partials * kClusterSmall), kClusterSmall);
     if (s4.long_ctas > sp.long_ctas) {

@@ -128,7 +128,7 @@ def test_config4_batch8_256k_skewed_decode(cuda_device):
 def test_decode_group7_batch8_clusters_of_4(cuda_device):
     """Qwen2.5-7B heads (28 / 4, group 7), batch 8, every KV head retrieval,
     16,384 cached tokens: 32 split units, which the plan runs in clusters of 4
-    (clusters of 8 would leave fewer than 2.25 streaming CTAs per SM).  A
+    (clusters of 8 would leave fewer than 2 streaming CTAs per SM).  A
     cluster CTA's output slice (7 x 128 / 4 = 224 outputs) is longer than the
     CTA, so its threads combine two outputs each.  Every unit against the oracle."""
     Hq, G, B, D, T, sink, recent = 28, 4, 8, 128, 16384, 128, 256
