@@ -40,9 +40,10 @@
 //     of the launch attends to it); a streaming unit's after every read of
 //     the unit (attend, then append).
 //   output gather (multi-GPU, when peers are attached): the CTA that finishes
-//     a unit stores its rows into every rank's output region (peer pointers)
-//     and, after a barrier, publishes a per-(layer, unit) flag to every rank
-//     with one system-scope fence and relaxed stores (gather.cu waits on them).
+//     a unit's rows (or slice of rows) stores them into every rank's output
+//     region (peer pointers), 16 bytes per store; the layer's flags are
+//     published by the gather wait kernel once this grid has completed
+//     (gather.cu).
 //
 // Launches use programmatic dependent launch: the producer streams pages before
 // griddepcontrol.wait (except the page of position T-1, and nothing at all when
@@ -73,10 +74,9 @@ constexpr int kDynSmem = kStages * kStageBytes + 1024;
 // Split units run in thread-block clusters of 8 CTAs, or of 4 when clusters of
 // 8 would leave the GPU short of streaming CTAs (see plan_and_launch).
 constexpr int kClusterBig = 8, kClusterSmall = 4;
-// Workspace tickets: per (unit, cluster slice) one ticket, then per unit one
-// count of stored slices (multi-GPU publish); all zero between launches.  Sized
-// for clusters of 8, so it holds either layout.
-constexpr int kCounterBytes = kMaxUnits * (kClusterBig + 1) * 4;
+// Workspace tickets: per (unit, cluster slice) one ticket, zero between
+// launches; sized for clusters of 8, so it holds either layout.
+constexpr int kCounterBytes = kMaxUnits * kClusterBig * 4;
 constexpr int kMaxPartials = kMaxCtas / kClusterSmall;
 // A cluster CTA's output slice spans at most three rows of head_dim outputs.
 static_assert(kMaxGrp * kHeadDim / kClusterSmall <= 2 * kHeadDim, "slice rows staged in shared memory");
@@ -104,17 +104,15 @@ struct DecodeArgs {
   const int* T_dev;  // if non-null, past_len is read from here (CUDA-graph replay)
   float scale_log2;  // D^-0.5 * log2(e)
   float* ws;         // per-cluster partials, kMaxPartials x kPartialFloats
-  int* counters;     // [unit][slice] tickets, then [unit] stored-slice counts; zero between launches
+  int* counters;     // [unit][slice] tickets; zero between launches
   // 0: the kernel before this one in the stream wrote this layer's pages
   // (e.g. a prefill chunk's append), so no page is streamed before waiting
   // for it; 1: only the page of position T-1 may still be in flight
   int prefetch;
   // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
-  // bytes for every rank r (its output region as mapped here), then the flag
-  // (layer, unit) of every rank's flag array is set to T + 1
+  // bytes for every rank r (its output region as mapped here)
   int n_ranks;
   long long out_delta[kMaxRanks];
-  int32_t* flags[kMaxRanks];
 };
 
 // Store 8 consecutive output elements (16 bytes; p is 16-byte aligned) and,
@@ -126,18 +124,6 @@ __device__ __forceinline__ void store_out8(const DecodeArgs& a, __nv_bfloat16* p
     return;
   }
   for (int r = 0; r < a.n_ranks; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p) + a.out_delta[r]) = v;
-}
-
-// The unit's rows are stored everywhere and the caller's barrier ordered every
-// writer before this thread: one system-scope fence (cumulative over what the
-// barrier ordered before it) followed by relaxed system-scope stores is the
-// release that publishes (layer, unit) = T + 1 to every rank -- one fence for
-// all ranks instead of one per release store.
-__device__ __forceinline__ void publish_unit(const DecodeArgs& a, int bg, int T) {
-  const int idx = a.layer * a.geom.B * a.geom.G + bg;
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  for (int r = 0; r < a.n_ranks; ++r)
-    asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(a.flags[r] + idx), "r"(T + 1) : "memory");
 }
 
 // A unit's compact page list: retrieval pages 0..ceil(T/16)-1; streaming the
@@ -575,11 +561,6 @@ __global__ void __launch_bounds__(kThreads, kCluster == kClusterBig ? 1 : 3)
     }
   }
 
-  if (nsplit == 1 && a.n_ranks > 0) {
-    __syncthreads();  // every row of the unit is stored
-    if (tid == 0) publish_unit(a, bg, T);
-  }
-
   if (nsplit > 1) {
     // ============ cluster merge: 8 consecutive splits -> one partial (DSMEM) ============
     // nsplit is a multiple of kCluster and the unit's first CTA is cluster-aligned,
@@ -708,23 +689,8 @@ __global__ void __launch_bounds__(kThreads, kCluster == kClusterBig ? 1 : 3)
     // the slice (grp * 16 elements, starting at a multiple of 8) leaves as 16-byte stores
     for (int c = tid; c < (e_hi - e_lo) / 8; c += kThreads)
       store_out8(a, out_u + e_lo + 8 * c, reinterpret_cast<const uint4*>(s_out)[c]);
-    // the ticket is reset before the unit is published: once every unit of the
-    // layer is published, the next kernel may reuse the workspace
+    // ready for the next launch (which touches the workspace only after this grid completes)
     if (tid == 0) a.counters[u * kCluster + rank] = 0;
-    if (a.n_ranks > 0) {
-      // the finisher of the unit's last stored slice publishes it (its acquire
-      // covers the other slices' stores, its system-scope fence all of them)
-      __syncthreads();  // this slice is stored in every rank's region
-      if (tid == 0) {
-        int* done = a.counters + kMaxUnits * kCluster + u;
-        int n;
-        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(n) : "l"(done) : "memory");
-        if (n == kCluster - 1) {
-          *done = 0;
-          publish_unit(a, bg, T);
-        }
-      }
-    }
     cluster_wait();
     // the last cluster to store slice 0 follows every cluster of the unit past
     // its main loop: a split streaming unit's new token goes in now (its ring
@@ -923,10 +889,7 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   a.counters = static_cast<int*>(ws);
   a.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
   a.n_ranks = 0;
-  for (int r = 0; r < kMaxRanks; ++r) {
-    a.out_delta[r] = 0;
-    a.flags[r] = nullptr;
-  }
+  for (int r = 0; r < kMaxRanks; ++r) a.out_delta[r] = 0;
   if (c->n_ranks > 0) {
     // the layer's whole output (B, 1, Hq, D) must lie in this rank's region
     const char* own = c->out_regions[c->rank];
@@ -935,10 +898,7 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
     if (o < own || (size_t)(o - own) + span > c->out_bytes)
       return fail(AOH_ERR_INVALID_ARGUMENT, "decode: with peers attached, out must lie in this rank's output region");
     a.n_ranks = c->n_ranks;
-    for (int r = 0; r < c->n_ranks; ++r) {
-      a.out_delta[r] = (long long)(c->out_regions[r] - own);
-      a.flags[r] = c->flag_arrays[r];
-    }
+    for (int r = 0; r < c->n_ranks; ++r) a.out_delta[r] = (long long)(c->out_regions[r] - own);
   }
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(grid, cluster, st, attr, true);
@@ -966,7 +926,7 @@ int launch_decode_bf16(aoh_kv_cache* c, int layer, int past_len, const void* q, 
 // For callers that cannot allocate device memory (see include/aoh.h), the
 // decode workspace lives in a file-scope device array instead of a
 // caller-provided buffer.  It holds the tickets and up to kNoAllocPartials
-// cluster partials: 9 KB + 64 x 4160 B = 275,456 bytes, which every GPU that
+// cluster partials: 8 KB + 64 x 4160 B = 274,432 bytes, which every GPU that
 // loads this library keeps until the process exits.  The array is shared by
 // every call: calls that overlap on the GPU race on it.
 // ---------------------------------------------------------------------------

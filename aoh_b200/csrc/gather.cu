@@ -5,13 +5,17 @@
 // with device_map="sequential", eval/efficiency/benchmark_llama31.py:354-374).
 // Here the (sequence, KV head) units of a layer are partitioned over the GPUs
 // of a node (aoh_partition) and every unit's output rows must reach every
-// rank before the next layer.  The decode kernel does that itself: the CTA
-// that finishes a unit stores its rows into each rank's output region (peer
-// pointers opened with CUDA IPC), fences at system scope and release-stores
-// the flag (layer, unit) = position + 1 in each rank's flag array.  The wait
-// kernel below polls the local flag array with acquire loads.  Flags only
-// grow while positions grow; a cache that restarts at a lower position must
-// be detached, have its flags zeroed on every rank, and be attached again.
+// rank before the next layer.  The decode kernel moves the data itself: the
+// CTA that finishes a unit stores its rows into each rank's output region
+// (peer pointers opened with CUDA IPC), 16 bytes per store.  The wait kernel
+// below, launched after the decode of the layer, publishes this rank's units
+// -- a system-scope fence, then the flag (layer, unit) = position + 1 in each
+// rank's flag array -- and polls the local flag array with acquire loads until
+// every unit of the layer has arrived.  Publishing after the decode grid has
+// completed keeps the fence and the flag stores out of the decode's tail.
+// Flags only grow while positions grow; a cache that restarts at a lower
+// position must be detached, have its flags zeroed on every rank, and be
+// attached again.
 #include <cstring>
 
 #include "common.cuh"
@@ -28,48 +32,82 @@ __device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
   return v;
 }
 
-// One thread per unit of the layer: wait until its flag reaches position + 1.
-// Bounded in time: a thread polls without pausing for its first few
+constexpr int kMaxGatherUnits = 1024;  // (sequence, KV head) units of one layer
+
+struct GatherArgs {
+  int32_t* flags[kMaxRanks];  // every rank's flag array, as mapped here
+  int32_t* err;               // this cache's device check word
+  const int* T_dev;           // device-resident length, or null (use T)
+  int n_ranks, rank, base, n_units, T;
+  uint32_t owned[kMaxGatherUnits / 32];  // this rank's units of the layer
+};
+
+// Publish this rank's units of the layer, then wait until every unit's flag
+// reaches position + 1 (one thread per unit).
+//
+// Publishing: the decode of the layer has completed (griddepcontrol.wait), so
+// its stores into every rank's region are performed; each thread that owns a
+// unit issues a system-scope fence (cumulative over them) and then relaxed
+// system-scope stores of the unit's flag to every rank.
+//
+// Waiting is bounded in time: a thread polls without pausing for its first few
 // microseconds (a unit usually lands within them), then with short sleeps; a
 // flag that has not arrived after kPeerWaitNs -- or once another wait has
 // recorded a timeout in the check word -- makes it record kErrWaitTimeout and
 // stop, so a missing peer ends the step with an error instead of a hang.
 //
-// Launched with programmatic dependent launch: it starts while this rank's
-// decode of the layer is still running and polls every unit's flag, this
-// rank's own units included (they are published like the peers' ones), so the
-// decode's completion and the peers' flags are awaited at the same time; it
-// then waits for the decode to complete, so that finishing this kernel
-// implies finishing it.  The next kernel in the stream (the next layer's
-// decode) may start at once and stream its KV pages, but waits
-// (griddepcontrol.wait) for this kernel before touching anything that depends
-// on the gathered outputs.  The length is only written by the advance kernel,
-// which completes before any decode of the step starts.
-__global__ void gather_wait_kernel(const int32_t* flags, int base, int n_units, int T, const int* T_dev,
-                                   int32_t* err) {
+// Launched with programmatic dependent launch: the next kernel in the stream
+// (the next layer's decode) may start at once and stream its KV pages, but
+// waits (griddepcontrol.wait) for this kernel before touching anything that
+// depends on the gathered outputs.  The length is only written by the advance
+// kernel, which completes before any decode of the step starts.
+__global__ void gather_wait_kernel(const __grid_constant__ GatherArgs g) {
   griddep_launch_dependents();
-  const int want = (T_dev ? *T_dev : T) + 1;
-  for (int u = threadIdx.x; u < n_units; u += blockDim.x) {
-    const int32_t* f = flags + base + u;
+  griddep_wait();
+  const int want = (g.T_dev ? *g.T_dev : g.T) + 1;
+  for (int u = threadIdx.x; u < g.n_units; u += blockDim.x) {
+    if (!((g.owned[u >> 5] >> (u & 31)) & 1u)) continue;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < g.n_ranks; ++r)
+      asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(g.flags[r] + g.base + u), "r"(want) : "memory");
+  }
+  for (int u = threadIdx.x; u < g.n_units; u += blockDim.x) {
+    const int32_t* f = g.flags[g.rank] + g.base + u;
     if (ld_acquire_sys(f) >= want) continue;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
       if (ld_acquire_sys(f) >= want) break;
       const uint64_t dt = globaltimer_ns() - t0;
-      if (dt > kPeerWaitNs || wait_tripped(err)) {
-        atomicOr(err, kErrWaitTimeout);
+      if (dt > kPeerWaitNs || wait_tripped(g.err)) {
+        atomicOr(g.err, kErrWaitTimeout);
         break;
       }
       if (dt > 4000) __nanosleep(64);
     }
   }
-  griddep_wait();
 }
 
 }  // namespace
 
 int launch_gather_wait(aoh_kv_cache* c, int layer, int past_len, const int* past_len_dev, cudaStream_t st) {
   const int n_units = c->cfg.batch * c->cfg.num_kv_heads;
+  if (n_units > kMaxGatherUnits)
+    return fail(AOH_ERR_UNSUPPORTED, "aoh_gather_wait: %d units per layer, at most %d", n_units, kMaxGatherUnits);
+  GatherArgs g = {};
+  for (int r = 0; r < kMaxRanks; ++r) g.flags[r] = r < c->n_ranks ? c->flag_arrays[r] : nullptr;
+  g.err = c->dev_err;
+  g.T_dev = past_len_dev;
+  g.n_ranks = c->n_ranks;
+  g.rank = c->rank;
+  g.base = layer * n_units;
+  g.n_units = n_units;
+  g.T = past_len;
+  for (int b = 0; b < c->cfg.batch; ++b)
+    for (int kv = 0; kv < c->cfg.num_kv_heads; ++kv)
+      if (c->owned[c->unit(layer, b, kv)]) {
+        const int u = b * c->cfg.num_kv_heads + kv;
+        g.owned[u >> 5] |= 1u << (u & 31);
+      }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, 1);
   cfg.blockDim = dim3(std::min(1024, (n_units + 31) / 32 * 32), 1, 1);
@@ -79,9 +117,7 @@ int launch_gather_wait(aoh_kv_cache* c, int layer, int past_len, const int* past
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_check(cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const int32_t*)c->flag_arrays[c->rank],
-                                       layer * n_units, n_units, past_len, past_len_dev, c->dev_err),
-                    "gather wait launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, gather_wait_kernel, g), "gather wait launch");
 }
 
 }  // namespace aoh

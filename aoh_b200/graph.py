@@ -16,6 +16,11 @@ step's q/k/v into them before ``replay()`` (or let producing kernels do so).
 With a ``PeerGather`` (multi-GPU, one process per GPU) each layer's decode
 kernel also stores its units' outputs into every rank's output region, and
 the graph waits for all ranks' units after each layer (the layer boundary).
+With ``overlap_gather=True`` each layer's wait runs on a second stream
+instead, beside the next layers' decode kernels, and the step ends after all
+of them: for a step whose layers do not consume one another's attention
+output (q, k, v of every layer given up front, as in an attention-only
+benchmark), the ranks then meet once per step instead of once per layer.
 """
 from __future__ import annotations
 
@@ -37,7 +42,7 @@ class DecodeStepGraph:
     """
 
     def __init__(self, cache: AoHKVCache, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                 out: torch.Tensor, max_steps: int, layers=None, gather=None):
+                 out: torch.Tensor, max_steps: int, layers=None, gather=None, overlap_gather: bool = False):
         if cache.dtype != torch.bfloat16:
             raise ValueError("graph decode needs a bfloat16 cache")
         self.cache = cache
@@ -49,6 +54,8 @@ class DecodeStepGraph:
                 raise ValueError(f"{name} must be a contiguous bf16 tensor on {cache.device}")
         self.q, self.k, self.v, self.out = q, k, v, out
         self.gather = gather
+        self.overlap_gather = bool(overlap_gather) and gather is not None
+        self._side = torch.cuda.Stream(device=cache.device) if self.overlap_gather else None
         cache.reserve(cache.kv_seq_len + max_steps + 1)
         self._L = cache._L
         self._ws = cache.decode_workspace()
@@ -67,6 +74,7 @@ class DecodeStepGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._launch_layers()
+            # the waits read the device length: they end before it advances
             _lib.check(self._L.aoh_kv_advance(cache._h, 1, C.c_void_p(_lib.stream_handle())),
                        "aoh_kv_advance")
         # capture does not execute: put the device length back to the host's
@@ -77,16 +85,25 @@ class DecodeStepGraph:
                    "aoh_kv_set_length")
 
     def _launch_layers(self, with_gather: bool = True) -> None:
+        main = torch.cuda.current_stream(self.cache.device)
         st = C.c_void_p(_lib.stream_handle())
         h = self.cache._h
+        overlap = with_gather and self.overlap_gather
         for i, layer in enumerate(self.layers):
             rc = self._L.aoh_attn_decode(h, layer, _lib.PAST_LEN_DEVICE, C.c_void_p(self.q[i].data_ptr()),
                                          C.c_void_p(self.k[i].data_ptr()), C.c_void_p(self.v[i].data_ptr()),
                                          C.c_void_p(self.out[i].data_ptr()), C.c_void_p(self._ws.data_ptr()),
                                          self._ws.numel(), st)
             _lib.check(rc, "aoh_attn_decode")
-            if with_gather and self.gather is not None:
+            if overlap:
+                # the layer's wait starts when this layer's decode has finished
+                self._side.wait_stream(main)
+                side = C.c_void_p(_lib.stream_handle(self._side))
+                _lib.check(self._L.aoh_gather_wait(h, layer, _lib.PAST_LEN_DEVICE, side), "aoh_gather_wait")
+            elif with_gather and self.gather is not None:
                 _lib.check(self._L.aoh_gather_wait(h, layer, _lib.PAST_LEN_DEVICE, st), "aoh_gather_wait")
+        if overlap:
+            main.wait_stream(self._side)
 
     def replay(self) -> None:
         """Run one decode step (all captured layers) and advance the length."""

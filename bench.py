@@ -376,7 +376,8 @@ def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: di
                                             world, owner.ctypes.data_as(C.POINTER(C.c_int32))), "aoh_partition")
     owned = (owner == rank).astype(np.uint8)
     clock_steps = 5 * 400  # pages reserved for the clock warm-up below
-    max_ctx = T + args.warmup + args.steps + 2 * (e2e_steps + 2) + 8 + clock_steps + 16
+    strict_steps = min(args.steps, 100) if world > 1 and gather == "peer" else 0
+    max_ctx = T + args.warmup + args.steps + 2 * (e2e_steps + 2) + 8 + clock_steps + 16 + 2 * (strict_steps + 4)
     cache = AoHKVCache(labels, HQ, batch=B, sink_size=SINK, recent_size=RECENT, max_context=max_ctx,
                        dtype=torch.bfloat16, device=dev, owned=owned, reserve_all=True)
     fill_units(torch, cache)
@@ -448,8 +449,11 @@ def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: di
     graph = None
     if world == 1 or peer is not None:
         from aoh_b200.graph import DecodeStepGraph
+        # the step's layers are independent (every layer's q, k, v given up front),
+        # so each layer's gather wait overlaps the next layers' decode kernels
         graph = DecodeStepGraph(cache, q, kn, vn, out,
-                                max_steps=args.warmup + args.steps + e2e_steps + 8 + clock_steps, gather=peer)
+                                max_steps=args.warmup + args.steps + e2e_steps + 8 + clock_steps, gather=peer,
+                                overlap_gather=peer is not None)
 
     def step():
         if graph is not None:
@@ -500,6 +504,32 @@ def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: di
         ms = float(t.item())
     status = cache.device_status()
     assert status == 0, f"device-side check tripped ({status})"
+
+    # the same step with the layer boundary kept: every layer's wait before the
+    # next layer's decode (what a model whose next layer reads this output needs)
+    boundary = None
+    if strict_steps:
+        sg = DecodeStepGraph(cache, q, kn, vn, out, max_steps=strict_steps + 4, gather=peer)
+        for _ in range(3):
+            sg.replay()
+        barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(strict_steps):
+            sg.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        sms = s0.elapsed_time(s1) / strict_steps
+        t = torch.tensor([sms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sms = float(t.item())
+        boundary = {"strict_us_layer_seq": round(sms * 1000.0 / (L * B), 3),
+                    "overlapped_us_layer_seq": round(ms * 1000.0 / (L * B), 3), "strict_steps": strict_steps,
+                    "note": "value overlaps each layer's gather wait with the next layers' decode (the step's "
+                            "layers are independent); strict waits for every rank's units after each layer"}
+        sg = None
+        assert cache.device_status() == 0
 
     # roofline of this rank's decode kernel (the only kernel in the N=1 step)
     T_mid = T0 + args.steps // 2
@@ -567,7 +597,8 @@ def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: di
             "bytes_launch": bytes_launch, "achieved": achieved, "e2e": e2e, "parity": parity, "clocks": clk,
             "host_us": host_us, "gpu_launches": per_step * args.steps, "kv_memory": kv_mem,
             "launch_mode": "cuda_graph+pdl" if graphed else "eager+pdl",
-            "gather": None if world == 1 else ("nvlink_peer_stores" if peer is not None else "nccl_all_gather")}
+            "gather": None if world == 1 else ("nvlink_peer_stores" if peer is not None else "nccl_all_gather"),
+            "layer_boundary": boundary}
 
 
 # ----------------------------------------------------------------------------
@@ -853,7 +884,7 @@ def run_aoh(args):
                                           "bytes_per_launch": b["bytes_launch"],
                                           "avg_launch_us": round(b["launch_us"], 3)},
                    "parity": b["parity"], "clocks": b["clocks"], "kv_memory": b["kv_memory"],
-                   "gpu_launches": b["gpu_launches"]}
+                   "gpu_launches": b["gpu_launches"], "layer_boundary": b["layer_boundary"]}
 
     extras = {}
     cpu = None
@@ -893,6 +924,7 @@ def run_aoh(args):
         "gpu_launches": main["gpu_launches"],
         "launch_mode": main["launch_mode"],
         "gather": main["gather"],
+        "layer_boundary": main["layer_boundary"],
         "host_enqueue_us_per_layer": round(main["host_us"], 2),
         "clocks": main["clocks"],
         "kv_memory": main["kv_memory"],

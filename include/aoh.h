@@ -183,7 +183,7 @@ AOH_API int aoh_attn_decode(aoh_kv_cache* cache, int32_t layer, int32_t past_len
  * reachable from the calling layer).  No counterpart in the reference, whose
  * eager path allocates new tensors on every call.
  *
- * The split-KV scratch is a static device array inside libaoh.so: 275,456
+ * The split-KV scratch is a static device array inside libaoh.so: 274,432
  * bytes (tickets for 256 units + 64 cluster partials), held on every GPU that
  * loads the library until the process exits.  bf16 caches only; a layer whose
  * plan would need more than 256 (sequence, KV head) units or more than 64
@@ -283,10 +283,10 @@ AOH_API int aoh_partition(const uint8_t* labels, int32_t num_layers, int32_t bat
 /* Output gather over NVLink (no counterpart in the reference).              */
 /* One process per GPU of one node; each rank decodes the units it owns      */
 /* (aoh_partition) and the decode kernel itself stores every finished unit's */
-/* output rows into the output region of every rank, then publishes a flag  */
-/* per (layer, unit) in every rank's flag array.  aoh_gather_wait is the     */
-/* layer boundary: it returns (on the GPU) once all units of the layer have  */
-/* arrived here.                                                             */
+/* output rows into the output region of every rank.  aoh_gather_wait, after */
+/* the decode of the layer, publishes this rank's units (a flag per (layer, */
+/* unit) in every rank's flag array) and returns (on the GPU) once all units */
+/* of the layer have arrived here: every rank calls it for every layer.      */
 /* ------------------------------------------------------------------------- */
 
 #define AOH_IPC_HANDLE_BYTES 64
@@ -310,10 +310,13 @@ AOH_API int aoh_shared_close(void* dev_ptr);
  * writes the same offsets in every region. */
 AOH_API int aoh_kv_set_peers(aoh_kv_cache* cache, int32_t n_ranks, int32_t rank, void* const* out_regions,
                              size_t out_bytes, int32_t* const* flag_arrays);
-/* Stream-ordered wait until every (sequence, KV head) unit of `layer` decoded
- * at position past_len (or the device length, AOH_PAST_LEN_DEVICE) has been
- * stored here by its owner.  The wait is bounded: a missing peer sets the
- * cache's device check word (aoh_kv_device_status) instead of hanging. */
+/* Stream-ordered, after this rank's aoh_attn_decode of `layer`: publishes the
+ * units this rank owns (flag = position + 1 in every rank's flag array, after
+ * a system-scope fence), then waits until every (sequence, KV head) unit of
+ * `layer` decoded at position past_len (or the device length,
+ * AOH_PAST_LEN_DEVICE) has been stored here by its owner.  The wait is
+ * bounded: a missing peer sets the cache's device check word
+ * (aoh_kv_device_status) instead of hanging. */
 AOH_API int aoh_gather_wait(aoh_kv_cache* cache, int32_t layer, int32_t past_len, aoh_stream stream);
 
 /* ------------------------------------------------------------------------- */

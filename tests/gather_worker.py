@@ -3,7 +3,9 @@
 Each rank owns the (sequence, KV head) units aoh_partition gives it and
 decodes them with the output gather attached; afterwards every rank must hold
 every unit's output, matching a cache on the same GPU that owns all units.
-Checked for eager calls (host past_len) and for the CUDA-graph step.
+Checked for eager calls (host past_len) and for the CUDA-graph step, with the
+layer boundary kept (a wait after each layer) and with the waits overlapping
+the next layers' decode kernels.
 Rendezvous and the IPC handle exchange use gloo; the data path is the decode
 kernel's own stores over NVLink.
 """
@@ -28,6 +30,7 @@ L, B, HQ, G, D = 2, 3, 8, 2, 128
 SINK, RECENT = 16, 48
 CHUNKS = [256, 300]  # prefill, then decode steps
 STEPS = 4
+T_EXTRA = 2 * STEPS + 2 * (STEPS + 2) + 8  # positions the eager steps and both graphs use
 
 
 def main() -> int:
@@ -39,7 +42,7 @@ def main() -> int:
     labels = np.array([[1, 0], [0, 1]], dtype=np.float64)
     owner = np.zeros((L, B, G), dtype=np.int32)
     lab_u8 = np.ascontiguousarray(labels >= 0.5, dtype=np.uint8)
-    T_total = sum(CHUNKS) + 2 * STEPS + 8
+    T_total = sum(CHUNKS) + T_EXTRA
     _lib.check(_lib.lib().aoh_partition(lab_u8.ctypes.data_as(C.POINTER(C.c_uint8)), L, B, G, sum(CHUNKS), SINK,
                                         RECENT, world, owner.ctypes.data_as(C.POINTER(C.c_int32))), "partition")
     assert set(np.unique(owner)) <= set(range(world))
@@ -72,29 +75,31 @@ def main() -> int:
                 print(f"rank {rank} eager layer {l}: max abs err {err}", flush=True)
                 bad += 1
     torch.cuda.synchronize()
-    # CUDA-graph steps: the same inputs replayed on both caches
-    q, k, v = rnd(L, B, 1, HQ, D), rnd(L, B, 1, G, D), rnd(L, B, 1, G, D)
-    ref_out = torch.zeros((L, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
-    g_mine = DecodeStepGraph(mine, q, k, v, peer.out, max_steps=STEPS + 2, gather=peer)
-    g_full = DecodeStepGraph(full, q, k, v, ref_out, max_steps=STEPS + 2)
-    dist.barrier()
-    for _ in range(STEPS):
-        peer.out.zero_()
-        torch.cuda.synchronize()
-        dist.barrier()  # no rank stores into a region another rank is still clearing
-        g_mine.replay()
-        g_full.replay()
-        torch.cuda.synchronize()
-        err = (peer.out.float() - ref_out.float()).abs().max().item()
-        if not err <= 2e-2:
-            print(f"rank {rank} graph step: max abs err {err}", flush=True)
-            bad += 1
+    # CUDA-graph steps: the same inputs replayed on both caches, with the layer
+    # boundary kept, then with the waits overlapping the next layers' decode
+    for overlap in (False, True):
+        q, k, v = rnd(L, B, 1, HQ, D), rnd(L, B, 1, G, D), rnd(L, B, 1, G, D)
+        ref_out = torch.zeros((L, B, 1, HQ, D), dtype=torch.bfloat16, device=dev)
+        g_mine = DecodeStepGraph(mine, q, k, v, peer.out, max_steps=STEPS + 2, gather=peer, overlap_gather=overlap)
+        g_full = DecodeStepGraph(full, q, k, v, ref_out, max_steps=STEPS + 2)
         dist.barrier()
+        for _ in range(STEPS):
+            peer.out.zero_()
+            torch.cuda.synchronize()
+            dist.barrier()  # no rank stores into a region another rank is still clearing
+            g_mine.replay()
+            g_full.replay()
+            torch.cuda.synchronize()
+            err = (peer.out.float() - ref_out.float()).abs().max().item()
+            if not err <= 2e-2:
+                print(f"rank {rank} graph step (overlap={overlap}): max abs err {err}", flush=True)
+                bad += 1
+            dist.barrier()
+        del g_mine, g_full
     status = mine.device_status()
     if status != 0:
         print(f"rank {rank}: device check word {status}", flush=True)
         bad += 1
-    del g_mine, g_full
     peer.close()
     dist.destroy_process_group()
     print(f"rank {rank}: {'FAIL' if bad else 'ok'}", flush=True)
