@@ -13,8 +13,9 @@ API and host logic follow the reference (aoh/classifier.py, aoh/effective_rank.p
   (:88-106).
 
 The spectra come from libaoh's batched kernels (``aoh_classify_eff_ranks``):
-Gram matrices, Cholesky whitening and a Jacobi eigen-solve in float64 -- more
-accurate than the reference's float32 ``eigvals``.  Aggregation (float64
+Gram matrices (in ``binary`` mode on the integer tensor cores, exact), Cholesky
+whitening and a Jacobi eigen-solve in float64 -- more accurate than the
+reference's float32 ``eigvals``.  Aggregation (float64
 mean/min/max over each KV group's query heads) and the per-layer choice of the
 ``round((1 - sparsity) * G)`` lowest-rank KV heads are the reference's own
 host arithmetic (classifier.py:102-128).  ``label_margins`` reports, per
@@ -68,7 +69,11 @@ def eff_ranks_from_weights(wq: torch.Tensor, wk: torch.Tensor, num_q_heads: int,
                                         C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()), ws.numel(),
                                         C.c_void_p(_lib.stream_handle()))
         _lib.check(rc, "aoh_classify_eff_ranks")
-        return out.cpu().numpy()
+        ranks = out.cpu().numpy()
+    if not np.all(np.isfinite(ranks)):
+        # a bounded device wait gave up: the affected heads' spectra are NaN
+        raise RuntimeError("aoh_classify_eff_ranks: a device wait timed out (non-finite effective ranks)")
+    return ranks
 
 
 def get_model_info(config) -> dict:

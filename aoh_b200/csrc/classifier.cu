@@ -13,8 +13,10 @@
 // eigenvalues equal those of the symmetric S = L^T KK L where QQ = L L^T
 // (Cholesky).  Pipeline, all batched over (layer, head):
 //   1. gram_kernel: every QQ_h and KK_g (bf16 rows, products exact in fp32,
-//      fp32 partial sums over 8-element chunks accumulated in fp64; in binary
-//      mode the sums of +-1 products are exact integers);
+//      fp32 partial sums over 8-element chunks accumulated in fp64); in binary
+//      mode gram_sign_i8_kernel instead: sign(W) as int8 on the integer tensor
+//      cores (tcgen05.mma kind::i8, int32 accumulators in tensor memory) --
+//      sums of -1/0/+1 products, exact integers either way;
 //   2. cholesky_kernel: QQ_h = L_h L_h^T in shared memory (fp64);
 //   3. gemm_f64_kernel twice: M = KK_g L_h, S = L_h^T M (fp64);
 //   4. jacobi_kernel: cyclic parallel Jacobi on S (fp64, round-robin pairs,
@@ -123,6 +125,143 @@ __global__ void __launch_bounds__(256) gram_kernel(const T* __restrict__ wq, con
       Gm[r * kD + c] = acc[i][j];
       if (ti != tj) Gm[c * kD + r] = acc[i][j];
     }
+}
+
+// ---------------------------------------------------------------------------
+// 1b. Binary mode on the integer tensor cores.  One CTA per (layer, head):
+// its 128 threads turn 128 columns of the head's 128 weight rows per step into
+// int8 signs, stored in the 128-byte-swizzled K-major layout (two stages);
+// warp 0 issues four tcgen05.mma kind::i8 (K = 32 each) per step into a
+// 128 x 128 int32 accumulator in tensor memory, which is read back as
+// doubles.  |entries| <= d_model, far inside int32.  Needs d_model % 128 == 0
+// and 16-byte aligned rows (the host uses gram_kernel otherwise).
+// ---------------------------------------------------------------------------
+constexpr int kI8Threads = 128;
+constexpr int kI8K = 128;            // K columns (int8 bytes) per stage and row
+constexpr int kI8Stage = kD * kI8K;  // 16 KB
+constexpr int kI8Smem = 2 * kI8Stage + 1024;
+// Instruction descriptor, kind::i8: D s32 (2), A and B signed 8-bit (1), both
+// K-major, M = N = 128.
+constexpr uint32_t kIdescI8 =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kD >> 3) << 17) | ((uint32_t)(kD >> 4) << 24);
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]  (kind::i8, one CTA); lane 0 of the
+// calling (converged) warp issues.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, l;\n\t.reg .u32 lid;\n\tmov.u32 lid, %%laneid;\n\tsetp.eq.u32 l, lid, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@l tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t sign_byte(float x) { return x > 0.f ? 0x01u : (x < 0.f ? 0xFFu : 0u); }
+__device__ __forceinline__ uint32_t signs4(float a, float b, float c, float d) {
+  return sign_byte(a) | (sign_byte(b) << 8) | (sign_byte(c) << 16) | (sign_byte(d) << 24);
+}
+// 16 consecutive weights (16-byte aligned) -> 16 int8 signs
+__device__ __forceinline__ uint4 signs16(const __nv_bfloat16* p) {
+  const uint4 x = __ldg(reinterpret_cast<const uint4*>(p)), y = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+  return make_uint4(signs4(bf16_lo(x.x), bf16_hi(x.x), bf16_lo(x.y), bf16_hi(x.y)),
+                    signs4(bf16_lo(x.z), bf16_hi(x.z), bf16_lo(x.w), bf16_hi(x.w)),
+                    signs4(bf16_lo(y.x), bf16_hi(y.x), bf16_lo(y.y), bf16_hi(y.y)),
+                    signs4(bf16_lo(y.z), bf16_hi(y.z), bf16_lo(y.w), bf16_hi(y.w)));
+}
+__device__ __forceinline__ uint4 signs16(const float* p) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 2), d = __ldg(q + 3);
+  return make_uint4(signs4(a.x, a.y, a.z, a.w), signs4(b.x, b.y, b.z, b.w), signs4(c.x, c.y, c.z, c.w),
+                    signs4(d.x, d.y, d.z, d.w));
+}
+
+// grid: L * (Hq + G), kI8Threads threads, kI8Smem bytes of dynamic shared memory.
+// A wait that gives up (err) leaves the head's Gram NaN.
+template <typename T>
+__global__ void __launch_bounds__(kI8Threads) gram_sign_i8_kernel(const T* __restrict__ wq, const T* __restrict__ wk,
+                                                                  int Hq, int G, int dm, double* __restrict__ gram,
+                                                                  int* err) {
+  extern __shared__ uint8_t i8_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(i8_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar_mma[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_ok, s_drain_err;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m = blockIdx.x % (Hq + G), l = blockIdx.x / (Hq + G);
+  const T* A = m < Hq ? wq + ((size_t)l * Hq + m) * kD * dm : wk + ((size_t)l * G + (m - Hq)) * kD * dm;
+  if (tid == 0) {
+    mbar_init(&bar_mma[0], 1);
+    mbar_init(&bar_mma[1], 1);
+    fence_mbar_init();
+    s_ok = 1;
+    s_drain_err = 0;
+  }
+  if (warp == 0) {
+    tmem_alloc(&s_tmem, kD);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int steps = dm / kI8K;
+  int issued = 0;  // steps whose MMAs were committed
+  for (int s = 0; s < steps; ++s) {
+    const int st = s & 1;
+    uint8_t* stage = smem + st * kI8Stage;
+    // the MMAs that read this stage two steps ago have completed
+    if (s >= 2 && tid == 0 && !mbar_wait(&bar_mma[st], ((s - 2) >> 1) & 1, err)) s_ok = 0;
+    __syncthreads();
+    if (!s_ok) break;
+    // (row, 16-column chunk) units: 8 consecutive threads read one row's 128 columns
+    for (int u = tid; u < kD * (kI8K / 16); u += kI8Threads) {
+      const int r = u >> 3, c = u & 7;
+      const uint4 v = signs16(A + (size_t)r * dm + (size_t)s * kI8K + c * 16);
+      *reinterpret_cast<uint4*>(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = v;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the signs, visible to the tensor cores
+    __syncthreads();
+    if (warp == 0) {
+      tc_fence_after();
+      const uint32_t a = smem_u32(stage);
+#pragma unroll
+      for (int k = 0; k < kI8K / 32; ++k) {
+        const uint64_t desc = smem_desc_sw128(a + k * 32, 16, 1024);
+        mma_i8(tmem, desc, desc, kIdescI8, (s > 0 || k > 0) ? 1u : 0u);
+      }
+      mma_commit(&bar_mma[st]);
+    }
+    issued = s + 1;
+  }
+  // every MMA issued has completed: the last commit tracks all earlier ones.
+  // After a give-up this still waits (bounded, on a word of its own, which the
+  // recorded timeout does not cut short) before the tensor memory is freed.
+  if (tid == 0 && issued > 0) {
+    const int last = issued - 1;
+    int* e = s_ok ? err : &s_drain_err;
+    if (!mbar_wait(&bar_mma[last & 1], (last >> 1) & 1, e)) {
+      s_ok = 0;
+      if (e != err) atomicOr(err, kErrWaitTimeout);
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = s_ok != 0;
+  double* Gm = gram + ((size_t)l * (Hq + G) + m) * kMat;
+  const int row = warp * 32 + lane;  // tensor-memory lane = accumulator row
+#pragma unroll 1
+  for (int cb = 0; cb < kD / 32; ++cb) {
+    uint32_t v[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb * 32, v);
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      Gm[(size_t)row * kD + cb * 32 + j] = ok ? (double)(int)v[j] : __longlong_as_double(0x7ff8000000000000LL);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kD);
 }
 
 // ---------------------------------------------------------------------------
@@ -356,11 +495,14 @@ __global__ void __launch_bounds__(256) jacobi_kernel(const double* __restrict__ 
   }
 }
 
-size_t ws_bytes(int L, int Hq, int G) {
+// Workspace: the Grams, M and S (doubles), then 256 bytes holding the int
+// check word of the binary-mode kernel's bounded waits.
+size_t ws_core_bytes(int L, int Hq, int G) {
   const size_t gram = (size_t)L * (Hq + G) * kMat * sizeof(double);
   const size_t mb = (size_t)L * Hq * kMat * sizeof(double);
   return gram + 2 * mb;
 }
+size_t ws_bytes(int L, int Hq, int G) { return ws_core_bytes(L, Hq, G) + 256; }
 
 }  // namespace
 }  // namespace aoh
@@ -409,13 +551,28 @@ int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_
                       "jacobi smem attribute");
   });
   if (rc) return rc;
-  if (dtype == AOH_BF16)
+  // binary mode on the integer tensor cores when the rows split into 128-column
+  // steps of 16-byte aligned loads (every model's d_model); otherwise SIMT
+  const bool on_i8 = binary && d_model % kI8K == 0 && reinterpret_cast<uintptr_t>(wq) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(wk) % 16 == 0;
+  if (on_i8) {
+    int* err = reinterpret_cast<int*>(static_cast<char*>(workspace) + ws_core_bytes(L, Hq, G));
+    rc = cuda_check(cudaMemsetAsync(err, 0, sizeof(int), st), "classifier: clear check word");
+    if (rc) return rc;
+    if (dtype == AOH_BF16)
+      gram_sign_i8_kernel<__nv_bfloat16><<<L * (Hq + G), kI8Threads, kI8Smem, st>>>(
+          static_cast<const __nv_bfloat16*>(wq), static_cast<const __nv_bfloat16*>(wk), Hq, G, d_model, gram, err);
+    else
+      gram_sign_i8_kernel<float><<<L * (Hq + G), kI8Threads, kI8Smem, st>>>(
+          static_cast<const float*>(wq), static_cast<const float*>(wk), Hq, G, d_model, gram, err);
+  } else if (dtype == AOH_BF16) {
     gram_kernel<__nv_bfloat16><<<dim3(3, L * (Hq + G)), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(wq), static_cast<const __nv_bfloat16*>(wk), Hq, G, d_model, binary, gram);
-  else
+  } else {
     gram_kernel<float><<<dim3(3, L * (Hq + G)), 256, 0, st>>>(static_cast<const float*>(wq),
                                                               static_cast<const float*>(wk), Hq, G, d_model,
                                                               binary, gram);
+  }
   cholesky_kernel<<<L * Hq, 256, kMat * sizeof(double), st>>>(gram, Hq, G);
   gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, mbuf, Hq, G, 0);
   gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, sbuf, Hq, G, 1);

@@ -103,3 +103,25 @@ def test_classifier_api_on_stub_model(cuda_device):
     assert np.array_equal(labels, z["fp32_mean_sp0.5_labels"])
     r = clf.compute_eff_rank(wq[0, :128], wk[0, :128])
     assert abs(r - z["fp32_eff_ranks_q"][0, 0]) <= 1e-4 * r
+
+
+@pytest.mark.parametrize("dm", [512, 320])
+def test_binary_ranks_exact(cuda_device, dm):
+    """Binary mode: the Gram matrices are sums of -1/0/+1 products, exact in
+    integers -- on the integer tensor cores when d_model is a multiple of 128
+    (512), in the SIMT kernel otherwise (320) -- so the effective ranks equal the
+    oracle's float64 restatement (exact Grams, symmetric eigen-solve) to within
+    one float32 ulp of the stored value.  Weights include exact zeros."""
+    from oracle import aoh_oracle as orc
+
+    L, Hq, G, D = 2, 8, 2, 128
+    rng = np.random.default_rng(dm)
+    w = rng.standard_normal((2, L, Hq * D, dm)).astype(np.float32)
+    w[:, :, :, ::7] = 0.0  # sign(0) = 0 must contribute nothing
+    wq = torch.from_numpy(w[0]).to(torch.bfloat16)
+    wk = torch.from_numpy(w[1, :, :G * D]).to(torch.bfloat16)
+    ranks = clf.eff_ranks_from_weights(wq.cuda(), wk.cuda(), Hq, G, D, binary=True)
+    want = orc.compute_all_eff_ranks([x.float().numpy() for x in wq], [x.float().numpy() for x in wk], Hq, G, D,
+                                     binary=True, exact=True)
+    ulp = np.spacing(np.abs(want).astype(np.float32)).astype(np.float64)
+    assert np.all(np.abs(ranks - want) <= ulp), np.max(np.abs(ranks - want) / ulp)
