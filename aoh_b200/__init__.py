@@ -13,10 +13,9 @@ from .classifier import AoHClassifier, compute_all_eff_ranks, compute_eff_rank, 
 from .io import load_results, save_results
 
 
-
 def __getattr__(name):
     # HF integration (imports transformers): loaded on first use
-    if name in ("patch_aoh_model", "AoHModelCache"):
+    if name in ("patch_aoh_model", "AoHModelCache", "ModelDecodeGraph"):
         from . import hf
         return getattr(hf, name)
     raise AttributeError(f"module 'aoh_b200' has no attribute {name!r}")
@@ -31,6 +30,7 @@ __all__ = [
     "compute_eff_rank",
     "label_margins",
     "patch_aoh_model",
+    "ModelDecodeGraph",
     "load_results",
     "pages_needed",
     "save_results",

@@ -59,6 +59,7 @@ _SIGNATURES = {
     "aoh_decode_workspace_bytes": (C.c_size_t, [_vp]),
     "aoh_kv_set_length": (C.c_int, [_vp, _i32, _vp]),
     "aoh_kv_advance": (C.c_int, [_vp, _i32, _vp]),
+    "aoh_kv_set_decode_append": (C.c_int, [_vp, _i32]),
     "aoh_attn_decode": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, C.c_size_t, _vp]),
     "aoh_attn_decode_noalloc": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "aoh_attn_prefill": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),

@@ -52,8 +52,15 @@ def aoh_attention(cache: AoHKVCache, layer_idx: int, q: torch.Tensor, k: torch.T
     _check_q(cache, q, q_len)
     if out is None:
         out = torch.empty_like(q)
-    past = cache.kv_seq_len
-    cache.reserve(past + q_len)
+    if cache.device_length:
+        # a captured decode step: the kernel reads the device-resident length,
+        # whose pages were reserved when the capture was set up
+        if q_len != 1:
+            raise ValueError("a cache in device-length mode takes decode steps (q_len 1) only")
+        past = _lib.PAST_LEN_DEVICE
+    else:
+        past = cache.kv_seq_len
+        cache.reserve(past + q_len)
     L = cache._L
     st = C.c_void_p(_lib.stream_handle())
     if q_len == 1:
@@ -70,7 +77,7 @@ def aoh_attention(cache: AoHKVCache, layer_idx: int, q: torch.Tensor, k: torch.T
         rc = fn(cache._h, layer_idx, past, q_len, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
                 C.c_void_p(v.data_ptr()), C.c_void_p(out.data_ptr()), st)
         _lib.check(rc, "aoh_attn_prefill_flash" if cache.backend == "flash" else "aoh_attn_prefill")
-    if advance and layer_idx == cache.num_layers - 1:
+    if advance and layer_idx == cache.num_layers - 1 and not cache.device_length:
         cache.kv_seq_len += q_len
     return out
 

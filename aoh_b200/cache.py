@@ -96,6 +96,10 @@ class AoHKVCache:
         self.n_ret = [int((labels[i] >= 0.5).sum()) for i in range(self.num_layers)]
         self.n_str = [self.num_kv_heads - n for n in self.n_ret]
         self.kv_seq_len = 0
+        # While True, decode calls read the device-resident length (set with
+        # aoh_kv_set_length, advanced by aoh_kv_advance) instead of kv_seq_len and
+        # leave kv_seq_len alone: how a captured decode step is recorded.
+        self.device_length = False
         self.owned = None if owned is None else np.ascontiguousarray(owned, dtype=np.uint8).reshape(
             self.num_layers, self.batch, self.num_kv_heads)
         if num_pages is None:

@@ -109,6 +109,7 @@ struct DecodeArgs {
   // (e.g. a prefill chunk's append), so no page is streamed before waiting
   // for it; 1: only the page of position T-1 may still be in flight
   int prefetch;
+  int append;  // 0: a dry run, the new token is not written
   // output gather (n_ranks > 0): a unit's rows are stored at out + out_delta[r]
   // bytes for every rank r (its output region as mapped here)
   int n_ranks;
@@ -343,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, kCluster == kClusterBig ? 1 : 3)
     // of this launch attends (every cached key it reads is below T, and a torn
     // read of that slot is masked like any unattended slot), so the unit's
     // first CTA writes it now, off the end of the kernel.
-    if (retr && split == 0 && cw == 0) append_token(a, uv, bt, b, g, lane);
+    if (a.append && retr && split == 0 && cw == 0) append_token(a, uv, bt, b, g, lane);
     // Q^T B-fragments: qf[kk][0] = Q[n][16kk+2c..+1], qf[kk][1] = Q[n][16kk+8+2c..+1], n = lane/4
     uint32_t qf[8][2];
     {
@@ -699,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, kCluster == kClusterBig ? 1 : 3)
   }
 
   // ===================== a streaming unit's new token (after every read of the unit) =====================
-  if (!retr && tid < 32) append_token(a, uv, bt, b, g, lane);
+  if (a.append && !retr && tid < 32) append_token(a, uv, bt, b, g, lane);
 }
 
 // Per device: the SM count and the CTAs resident at once when launched in
@@ -903,7 +904,8 @@ static int plan_and_launch(aoh_kv_cache* c, int layer, int past_len, const void*
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(grid, cluster, st, attr, true);
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
-  c->last_write_layer = layer;  // the kernel appends the new token to this layer
+  a.append = c->decode_append ? 1 : 0;
+  if (a.append) c->last_write_layer = layer;  // the kernel appends the new token to this layer
   return cuda_check(cluster == kClusterBig ? cudaLaunchKernelEx(&cfg, decode_bf16_kernel<kClusterBig>, a, plan)
                                            : cudaLaunchKernelEx(&cfg, decode_bf16_kernel<kClusterSmall>, a, plan),
                     "decode kernel launch");

@@ -101,6 +101,7 @@ struct aoh_kv_cache {
   // with its append, append) touched; a following kernel on another layer may
   // prefetch its pages before waiting for that kernel
   int last_write_layer = -1;
+  bool decode_append = true;  // false: decode calls attend without appending (aoh_kv_set_decode_append)
   // prefill scratch owned by the cache (grow-only; freed on destroy):
   // [prefill_cnt_cap ticket counters, padded to 256 B][split partials]; the
   // counters are zero between launches

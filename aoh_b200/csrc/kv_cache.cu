@@ -325,6 +325,12 @@ int aoh_kv_advance(aoh_kv_cache* c, int32_t n, aoh_stream stream) {
   return rc;
 }
 
+int aoh_kv_set_decode_append(aoh_kv_cache* c, int32_t enabled) {
+  if (!c) return fail(AOH_ERR_INVALID_ARGUMENT, "null cache");
+  c->decode_append = enabled != 0;
+  return AOH_OK;
+}
+
 int32_t aoh_kv_free_pages(const aoh_kv_cache* c) { return c ? (int32_t)c->free_list.size() : -1; }
 
 int aoh_kv_unit_pages(const aoh_kv_cache* c, int32_t layer, int32_t seq, int32_t kv_head,

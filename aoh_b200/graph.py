@@ -61,13 +61,18 @@ class DecodeStepGraph:
         self._ws = cache.decode_workspace()
         self._set_length(cache.kv_seq_len)
         # the first launch configures kernel attributes (not capturable): run the
-        # step once eagerly with the length not advanced -- it appends at the
-        # current position, which the first replay rewrites with the same data.
+        # step once eagerly as a dry run -- attend, no append (an append at the
+        # current position would already overwrite a streaming head's ring slot
+        # whose row the first replay, at the same position, still attends).
         # A gather is detached meanwhile: the eager step must publish no flags
         # the first replay (same position) would then find already set.
         if gather is not None:
             gather.detach()
-        self._launch_layers(with_gather=False)
+        _lib.check(self._L.aoh_kv_set_decode_append(cache._h, 0), "aoh_kv_set_decode_append")
+        try:
+            self._launch_layers(with_gather=False)
+        finally:
+            _lib.check(self._L.aoh_kv_set_decode_append(cache._h, 1), "aoh_kv_set_decode_append")
         torch.cuda.synchronize(cache.device)
         if gather is not None:
             gather.attach()

@@ -166,3 +166,83 @@ def patch_aoh_model(model, labels: np.ndarray, sink_size: int, recent_size: int)
         return AoHModelCache(paged)
 
     return make_cache, n_ret, n_str
+
+
+class ModelDecodeGraph:
+    """One decode step of a patched model -- every layer's projections,
+    QK-norm/RoPE, head-mixed attention and MLP, and the logits -- captured once
+    as a CUDA graph and replayed per token.
+
+    The reference decodes with eager Python over the layers
+    (eval/efficiency/benchmark_llama31.py:319-338); on the GPU that is mostly
+    launch overhead.  Captured here: the attention reads the cache's
+    device-resident length (``AoHKVCache.device_length``), a final kernel
+    advances it (the reference's ``kv_seq_len += 1``, :249-250), and the token
+    and its position are fixed tensors written before each replay.  Pages for
+    ``max_steps`` tokens are reserved up front.  ``step(token_ids)`` returns the
+    step's logits (B, 1, vocab) -- a tensor the next step overwrites.
+    """
+
+    def __init__(self, model, cache: AoHModelCache, max_steps: int):
+        import ctypes as C
+
+        from . import _lib
+
+        paged = cache.paged
+        if paged.dtype != torch.bfloat16:
+            raise ValueError("a captured decode step needs a bfloat16 cache")
+        if paged.backend != "eager" and paged.kv_seq_len == 0:
+            raise ValueError("prefill the prompt before capturing decode steps")
+        self.model, self.cache, self.paged = model, cache, paged
+        dev = paged.device
+        B = paged.batch
+        self.ids = torch.zeros((B, 1), dtype=torch.long, device=dev)
+        self.pos = torch.zeros((B, 1), dtype=torch.long, device=dev)
+        self.cpos = torch.zeros((1,), dtype=torch.long, device=dev)
+        paged.reserve(paged.kv_seq_len + max_steps + 1)
+        self._L, self._C = paged._L, C
+        self._set_length(paged.kv_seq_len)
+        self._inputs(torch.zeros((B, 1), dtype=torch.long, device=dev))
+        paged.device_length = True
+        try:
+            # the first launches configure kernels and workspaces (not capturable):
+            # one eager step at the current length as a dry run -- attend, no
+            # append (an append at this position would already overwrite a
+            # streaming head's ring slot whose row the first replay still attends)
+            _lib.check(self._L.aoh_kv_set_decode_append(paged._h, 0), "aoh_kv_set_decode_append")
+            try:
+                with torch.no_grad():
+                    self._forward()
+            finally:
+                _lib.check(self._L.aoh_kv_set_decode_append(paged._h, 1), "aoh_kv_set_decode_append")
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.no_grad(), torch.cuda.graph(self.graph):
+                self.logits = self._forward()
+                _lib.check(self._L.aoh_kv_advance(paged._h, 1, C.c_void_p(_lib.stream_handle())), "aoh_kv_advance")
+        finally:
+            paged.device_length = False
+        self._set_length(paged.kv_seq_len)  # capture does not execute: the device length is the host's again
+
+    def _set_length(self, n: int) -> None:
+        from . import _lib
+
+        _lib.check(self._L.aoh_kv_set_length(self.paged._h, n, self._C.c_void_p(_lib.stream_handle())),
+                   "aoh_kv_set_length")
+
+    def _inputs(self, token_ids: torch.Tensor) -> None:
+        t = self.paged.kv_seq_len
+        self.ids.copy_(token_ids.view(self.ids.shape), non_blocking=True)
+        self.pos.fill_(t)
+        self.cpos.fill_(t)
+
+    def _forward(self) -> torch.Tensor:
+        return self.model(input_ids=self.ids, position_ids=self.pos, cache_position=self.cpos,
+                          past_key_values=self.cache, use_cache=True).logits
+
+    def step(self, token_ids: torch.Tensor) -> torch.Tensor:
+        """Decode one token per sequence (token_ids: (B,) or (B, 1)) and advance."""
+        self._inputs(token_ids)
+        self.graph.replay()
+        self.paged.kv_seq_len += 1
+        return self.logits

@@ -161,6 +161,12 @@ AOH_API int aoh_kv_device_status(aoh_kv_cache* cache, int32_t* flags, aoh_stream
 #define AOH_PAST_LEN_DEVICE (-1)
 AOH_API int aoh_kv_set_length(aoh_kv_cache* cache, int32_t length, aoh_stream stream);
 AOH_API int aoh_kv_advance(aoh_kv_cache* cache, int32_t n, aoh_stream stream);
+/* enabled = 0: aoh_attn_decode / aoh_attn_decode_noalloc attend without
+ * appending the new token (a dry run) until re-enabled; default 1.  For the
+ * uncaptured first launch before capturing a decode step at the same position:
+ * an append there would already overwrite a streaming head's ring slot that
+ * the captured step still attends (its oldest window row). */
+AOH_API int aoh_kv_set_decode_append(aoh_kv_cache* cache, int32_t enabled);
 
 /* Upper bound of the workspace aoh_attn_decode needs (bytes). */
 AOH_API size_t aoh_decode_workspace_bytes(const aoh_kv_cache* cache);

@@ -247,6 +247,15 @@ def test_graph_decode_matches_eager_and_oracle(cuda_device):
     qb, kb, vb = qs[0].clone(), ks[0].clone(), vs[0].clone()
     ob = torch.empty_like(qb)
     g = DecodeStepGraph(graphed, qb, kb, vb, ob, max_steps=steps)
+    # the graph's uncaptured first launch is a dry run: it appended nothing, so
+    # each streaming unit's oldest window row (the ring slot an append at T
+    # would take) still equals the eager cache's
+    for l in range(L):
+        for kv in range(G):
+            if labels[l, kv] < 0.5:
+                a = graphed.read_rows(l, 0, kv, [T - 256, T - 1])
+                b = eager.read_rows(l, 0, kv, [T - 256, T - 1])
+                assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]), (l, kv)
     f = lambda t: t.float().cpu().numpy()
     for s in range(steps):
         want = torch.stack([aoh_attention(eager, l, qs[s][l], ks[s][l], vs[s][l]) for l in range(L)])

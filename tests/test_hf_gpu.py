@@ -127,3 +127,44 @@ def test_rope_qk_matches_the_model_functions(cuda_device, norm):
             ulp = torch.where(w == 0, torch.full_like(w, 2.0 ** -133), w.abs() * 2.0 ** -7)
             assert bool(((got.float() - w).abs() <= ulp).all())
             assert (got == want).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("kind", ["llama", "qwen3"])
+def test_decode_graph_matches_eager_steps(cuda_device, kind):
+    """ModelDecodeGraph (the whole decode step captured once, the attention on
+    the device-resident length) against the same patched model stepped eagerly
+    from the same cache contents, token by token: the appended K/V rows (post
+    RoPE) are bit-identical -- same positions, same kernels -- and the logits
+    agree up to the GEMMs' bf16 rounding (a captured cuBLAS call may use
+    another algorithm), at the tolerance of the unpatched-model test above."""
+    from aoh_b200.hf import ModelDecodeGraph, patch_aoh_model
+
+    model = _tiny(kind)
+    labels = np.array([[1, 0], [0, 1]], dtype=np.float64)
+    make_cache, _, _ = patch_aoh_model(model, labels, 16, 48)
+    ids = torch.randint(0, 128, (1, 300), generator=torch.Generator().manual_seed(5)).cuda()
+    caches = [make_cache(max_context=512) for _ in range(2)]
+    want, got = [], []
+    with torch.no_grad():
+        for c in caches:  # the same prompt in both caches (two chunks, past the window)
+            model(input_ids=ids[:, :160], past_key_values=c, use_cache=True)
+            model(input_ids=ids[:, 160:290], past_key_values=c, use_cache=True)
+        g = ModelDecodeGraph(model, caches[1], max_steps=16)
+        for t in range(290, 300):
+            want.append(model(input_ids=ids[:, t:t + 1], past_key_values=caches[0], use_cache=True).logits.float())
+            got.append(g.step(ids[:, t]).float().clone())
+    torch.cuda.synchronize()
+    assert caches[0].get_seq_length() == caches[1].get_seq_length() == 300
+    for c in caches:
+        assert c.paged.device_status() == 0
+    for layer in range(2):
+        for kv in range(2):
+            pos = [290, 295, 299] if labels[layer, kv] >= 0.5 else [295, 299]  # streaming: rows still held
+            ka, va = caches[0].paged.read_rows(layer, 0, kv, pos)
+            kb, vb = caches[1].paged.read_rows(layer, 0, kv, pos)
+            assert torch.equal(ka, kb) and torch.equal(va, vb), (layer, kv)
+    for t, (w, gl) in enumerate(zip(want, got)):
+        err = (w - gl).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(w.flatten(), gl.flatten(), dim=0).item()
+        print(f"step {t}: max abs err {err:.4f} (max |logit| {w.abs().max().item():.3f}), cosine {cos:.6f}")
+        assert err <= 0.05 * w.abs().max().item() and cos > 0.999, (t, err, cos)
