@@ -14,7 +14,7 @@ API and host logic follow the reference (aoh/classifier.py, aoh/effective_rank.p
 
 The spectra come from libaoh's batched kernels (``aoh_classify_eff_ranks``):
 Gram matrices (in ``binary`` mode on the integer tensor cores, exact), Cholesky
-whitening and a Jacobi eigen-solve in float64 -- more accurate than the
+whitening and a Householder-tridiagonal + bisection eigen-solve in float64 -- more accurate than the
 reference's float32 ``eigvals``.  Aggregation (float64
 mean/min/max over each KV group's query heads) and the per-layer choice of the
 ``round((1 - sparsity) * G)`` lowest-rank KV heads are the reference's own

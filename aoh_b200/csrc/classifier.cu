@@ -19,9 +19,9 @@
 //      sums of -1/0/+1 products, exact integers either way;
 //   2. cholesky_kernel: QQ_h = L_h L_h^T in shared memory (fp64);
 //   3. gemm_f64_kernel twice: M = KK_g L_h, S = L_h^T M (fp64);
-//   4. jacobi_kernel: cyclic parallel Jacobi on S (fp64, round-robin pairs,
-//      64 disjoint rotations per step), then the entropy -> effective rank,
-//      rounded to float32 like the reference's stored value.
+//   4. tridiag_eig_kernel: Householder reduction of S to tridiagonal form,
+//      its eigenvalues by bisection on Sturm counts (fp64), then the entropy
+//      -> effective rank, rounded to float32 like the reference's stored value.
 // The aggregation over GQA groups and the per-layer top-k stay on the host in
 // float64 exactly as aoh/classifier.py:102-128 does them.
 #include <cfloat>
@@ -34,7 +34,6 @@ namespace {
 
 constexpr int kD = 128;                 // head_dim
 constexpr int kMat = kD * kD;           // elements of one 128x128 matrix
-constexpr int kJPitch = kD + 1;         // padded row (doubles) in the Jacobi kernel
 
 // ---------------------------------------------------------------------------
 // 1. Gram matrices: G = A A^T for A = 128 rows x d_model (bf16), 64x64 tiles.
@@ -358,138 +357,132 @@ __global__ void __launch_bounds__(256) gemm_f64_kernel(const double* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// 4. Parallel cyclic Jacobi on S (symmetric, fp64) -> eigenvalues -> eff rank.
-// Round-robin schedule: in step r the pairs are (127, r) and
-// ((r + k) mod 127, (r - k) mod 127) for k = 1..63 -- 64 disjoint pairs, and
-// over 127 steps every pair exactly once.  Each step computes the 64
-// rotations from the current matrix, applies them to rows, then to columns.
-// Sweeps stop when the off-diagonal norm is below 1e-15 of the diagonal norm.
-// grid: L * Hq, 256 threads, 129x128 doubles of shared memory.
+// 4. Eigenvalues of every symmetric S by Householder reduction to tridiagonal
+// form and bisection (eigenvalues only, fp64).  Column k's reflector
+// H = I - tau v v^T (v = x - alpha e1, alpha = -sign(x0) |x|) is applied to the
+// trailing block as the rank-2 update A -= v w^T + w v^T with p = tau A v,
+// w = p - (tau/2)(v^T p) v: 4/3 n^3 flops per matrix against the Jacobi
+// sweeps' ~0.1 GFLOP.  Then thread i finds the i-th eigenvalue of the
+// tridiagonal matrix (d, e) by bisection on Sturm counts (the number of
+// eigenvalues below x from the LDL^T pivots, tiny pivots replaced as in
+// LAPACK's dstebz), from the Gershgorin interval, to the interval's width /
+// 2^52.  Both steps are backward stable: eigenvalue errors ~ eps |S|.
+// grid: L * Hq, 256 threads, 128 x 129 doubles of dynamic shared memory.
 // ---------------------------------------------------------------------------
-constexpr int kMaxSweeps = 30;
+constexpr int kTPitch = kD + 1;
+constexpr int kBisect = 52;
 
-__global__ void __launch_bounds__(256) jacobi_kernel(const double* __restrict__ sbuf, int Hq,
-                                                     double* __restrict__ eff_out) {
+// Sum over the block of 256 threads, returned to every thread (s_red: 8 doubles).
+__device__ __forceinline__ double block_sum256(double v, double* s_red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // s_red free from the previous use
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += s_red[w];
+  return t;
+}
+
+__global__ void __launch_bounds__(256) tridiag_eig_kernel(const double* __restrict__ sbuf,
+                                                          double* __restrict__ eff_out) {
   extern __shared__ double sm[];
-  double* S = sm;  // [128][kJPitch]
-  __shared__ double s_c[64], s_s[64];
-  __shared__ int s_p[64], s_q[64];
+  double* S = sm;  // [128][kTPitch]
+  __shared__ double s_v[kD], s_w[kD], s_d[kD], s_e2[kD];
   __shared__ double s_red[8];
-  __shared__ int s_done;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const double* Sg = sbuf + (size_t)blockIdx.x * kMat;
-  for (int e = tid; e < kMat; e += 256) S[(e / kD) * kJPitch + e % kD] = Sg[e];
+  for (int e = tid; e < kMat; e += 256) S[(e / kD) * kTPitch + e % kD] = Sg[e];
   __syncthreads();
 
-  for (int sweep = 0; sweep < kMaxSweeps; ++sweep) {
-    // convergence test: off-diagonal vs diagonal squared norms
-    double off = 0.0, dia = 0.0;
-    for (int e = tid; e < kMat; e += 256) {
-      const int i = e / kD, j = e % kD;
-      const double v = S[i * kJPitch + j];
-      if (i == j) dia += v * v; else off += v * v;
+  for (int k = 0; k < kD - 2; ++k) {
+    const int r0 = k + 1, m = kD - r0;  // trailing block [r0, kD)^2, column k below the diagonal has m entries
+    const double x = tid < m ? S[(r0 + tid) * kTPitch + k] : 0.0;
+    const double x0 = S[r0 * kTPitch + k];
+    const double tail = block_sum256(tid >= 1 && tid < m ? x * x : 0.0, s_red);
+    if (tail == 0.0) {  // already tridiagonal in this column (uniform: every thread has the same sums)
+      if (tid == 0) {
+        s_d[k] = S[k * kTPitch + k];
+        s_e2[k] = x0 * x0;
+      }
+      continue;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      off += __shfl_xor_sync(0xffffffffu, off, o);
-      dia += __shfl_xor_sync(0xffffffffu, dia, o);
-    }
-    if (lane == 0) s_red[warp] = off;
-    __syncthreads();
+    const double alpha = -copysign(sqrt(tail + x0 * x0), x0);
+    const double v0 = x0 - alpha;
+    const double tau = 2.0 / (tail + v0 * v0);
+    if (tid < m) s_v[tid] = tid == 0 ? v0 : x;
     if (tid == 0) {
-      double t = 0.0;
-      for (int w = 0; w < 8; ++w) t += s_red[w];
-      s_red[0] = t;
+      s_d[k] = S[k * kTPitch + k];
+      s_e2[k] = alpha * alpha;
     }
     __syncthreads();
-    const double off_tot = s_red[0];
+    // p = tau A v: two threads per row of the trailing block
+    double pi = 0.0;
+    const int row = tid >> 1, half = tid & 1;
+    if (row < m) {
+      const double* Ar = S + (r0 + row) * kTPitch + r0;
+      for (int j = half; j < m; j += 2) pi += Ar[j] * s_v[j];
+    }
+    pi += __shfl_xor_sync(0xffffffffu, pi, 1);
+    pi *= tau;
+    const double vp = block_sum256(row < m && half == 0 ? s_v[row] * pi : 0.0, s_red);
+    const double K = 0.5 * tau * vp;
+    if (row < m && half == 0) s_w[row] = pi - K * s_v[row];
     __syncthreads();
-    if (lane == 0) s_red[warp] = dia;
-    __syncthreads();
-    if (tid == 0) {
-      double t = 0.0;
-      for (int w = 0; w < 8; ++w) t += s_red[w];
-      s_done = off_tot <= 1e-30 * t;
+    // A -= v w^T + w v^T on the trailing block
+    for (int e = tid; e < m * m; e += 256) {
+      const int i = e / m, j = e - i * m;
+      S[(r0 + i) * kTPitch + r0 + j] -= s_v[i] * s_w[j] + s_w[i] * s_v[j];
     }
     __syncthreads();
-    if (s_done) break;
+  }
+  if (tid == 0) {
+    s_d[kD - 2] = S[(kD - 2) * kTPitch + kD - 2];
+    s_d[kD - 1] = S[(kD - 1) * kTPitch + kD - 1];
+    const double en = S[(kD - 1) * kTPitch + kD - 2];
+    s_e2[kD - 2] = en * en;
+    s_e2[kD - 1] = 0.0;
+  }
+  __syncthreads();
 
-    for (int r = 0; r < kD - 1; ++r) {
-      if (tid < 64) {
-        int p, q;
-        if (tid == 0) {
-          p = r;
-          q = kD - 1;
-        } else {
-          p = (r + tid) % (kD - 1);
-          q = (r - tid + (kD - 1)) % (kD - 1);
-        }
-        if (p > q) { const int t = p; p = q; q = t; }
-        const double app = S[p * kJPitch + p], aqq = S[q * kJPitch + q], apq = S[p * kJPitch + q];
-        double c = 1.0, s = 0.0;
-        if (fabs(apq) > 1e-300 && fabs(apq) > 1e-18 * sqrt(fabs(app * aqq))) {
-          const double theta = (aqq - app) / (2.0 * apq);
-          const double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
-          c = 1.0 / sqrt(t * t + 1.0);
-          s = t * c;
-        }
-        s_c[tid] = c;
-        s_s[tid] = s;
-        s_p[tid] = p;
-        s_q[tid] = q;
-      }
-      __syncthreads();
-      // rows: R_p <- c R_p - s R_q ; R_q <- s R_p + c R_q
-      for (int e = tid; e < 64 * kD; e += 256) {
-        const int k = e / kD, j = e % kD;
-        const double c = s_c[k], s = s_s[k];
-        if (s == 0.0) continue;
-        double* rp = S + s_p[k] * kJPitch;
-        double* rq = S + s_q[k] * kJPitch;
-        const double x = rp[j], y = rq[j];
-        rp[j] = c * x - s * y;
-        rq[j] = s * x + c * y;
-      }
-      __syncthreads();
-      // columns
-      for (int e = tid; e < 64 * kD; e += 256) {
-        const int k = e / kD, i = e % kD;
-        const double c = s_c[k], s = s_s[k];
-        if (s == 0.0) continue;
-        double* row = S + i * kJPitch;
-        const int p = s_p[k], q = s_q[k];
-        const double x = row[p], y = row[q];
-        row[p] = c * x - s * y;
-        row[q] = s * x + c * y;
-      }
-      __syncthreads();
+  // bisection: thread i < 128 finds the i-th smallest eigenvalue
+  double lam = 0.0;
+  if (tid < kD) {
+    double lo = 0.0, hi = 0.0, emax2 = 0.0;
+    for (int j = 0; j < kD; ++j) {
+      const double r = (j > 0 ? sqrt(s_e2[j - 1]) : 0.0) + (j < kD - 1 ? sqrt(s_e2[j]) : 0.0);
+      lo = j == 0 ? s_d[j] - r : fmin(lo, s_d[j] - r);
+      hi = j == 0 ? s_d[j] + r : fmax(hi, s_d[j] + r);
+      emax2 = fmax(emax2, s_e2[j]);
     }
+    const double pivmin = DBL_MIN * fmax(1.0, emax2);
+    for (int it = 0; it < kBisect; ++it) {
+      const double mid = 0.5 * (lo + hi);
+      int below = 0;
+      double q = s_d[0] - mid;
+      if (fabs(q) < pivmin) q = -pivmin;
+      below += q < 0.0;
+      for (int j = 1; j < kD; ++j) {
+        q = s_d[j] - mid - s_e2[j - 1] / q;
+        if (fabs(q) < pivmin) q = -pivmin;
+        below += q < 0.0;
+      }
+      if (below > tid) hi = mid; else lo = mid;
+    }
+    lam = 0.5 * (lo + hi);
   }
 
-  // eigenvalues are the diagonal; effective rank (effective_rank.py:77-85) in fp64
-  double sig = 0.0;
-  if (tid < kD) sig = sqrt(fabs(S[tid * kJPitch + tid]) + 1e-12);
-  double ssum = sig;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-  __syncthreads();
-  if (lane == 0) s_red[warp] = ssum;
-  __syncthreads();
-  double total = 0.0;
-  for (int w = 0; w < 8; ++w) total += s_red[w];
+  // effective rank (effective_rank.py:77-85) in fp64
+  const double sig = tid < kD ? sqrt(fabs(lam) + 1e-12) : 0.0;
+  const double total = block_sum256(sig, s_red);
   double hterm = 0.0;
   if (tid < kD && total >= 1e-12) {
     const double p = sig / total;
     hterm = -p * log(p + 1e-12);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) hterm += __shfl_xor_sync(0xffffffffu, hterm, o);
-  __syncthreads();
-  if (lane == 0) s_red[warp] = hterm;
-  __syncthreads();
+  const double H = block_sum256(hterm, s_red);
   if (tid == 0) {
-    double H = 0.0;
-    for (int w = 0; w < 8; ++w) H += s_red[w];
     const double eff = total < 1e-12 ? 1.0 : exp(H);
     eff_out[blockIdx.x] = (double)(float)eff;
   }
@@ -546,9 +539,9 @@ int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_
                                             kMat * (int)sizeof(double)),
                        "cholesky smem attribute");
     if (r) return r;
-    return cuda_check(cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kD * kJPitch * (int)sizeof(double)),
-                      "jacobi smem attribute");
+    return cuda_check(cudaFuncSetAttribute(tridiag_eig_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kD * kTPitch * (int)sizeof(double)),
+                      "eigen-solve smem attribute");
   });
   if (rc) return rc;
   // binary mode on the integer tensor cores when the rows split into 128-column
@@ -576,7 +569,7 @@ int aoh_classify_eff_ranks(const void* wq, const void* wk, int32_t dtype, int32_
   cholesky_kernel<<<L * Hq, 256, kMat * sizeof(double), st>>>(gram, Hq, G);
   gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, mbuf, Hq, G, 0);
   gemm_f64_kernel<<<dim3(4, L * Hq), 256, 0, st>>>(gram, mbuf, sbuf, Hq, G, 1);
-  jacobi_kernel<<<L * Hq, 256, kD * kJPitch * sizeof(double), st>>>(sbuf, Hq, eff_ranks_out);
+  tridiag_eig_kernel<<<L * Hq, 256, kD * kTPitch * sizeof(double), st>>>(sbuf, eff_ranks_out);
   return cuda_check(cudaGetLastError(), "classifier kernel launch");
 }
 
