@@ -203,3 +203,17 @@ def test_attention_entry_points_need_a_bound_cache():
     rc, h = _create(cfg)
     assert L.aoh_attn_decode_noalloc(h, 0, 0, buf, buf, buf, buf, None) == _lib.UNSUPPORTED
     L.aoh_kv_destroy(h)
+
+
+def test_decode_dry_run_switch():
+    """aoh_kv_set_decode_append: a null cache is an argument error; on a cache
+    it toggles (host state only, no CUDA call), any non-zero value enabling."""
+    L = _lib.lib()
+    assert L.aoh_kv_set_decode_append(None, 0) == _lib.INVALID
+    assert b"null cache" in L.aoh_last_error()
+    cfg, keep = _cfg([[1, 0]])
+    rc, h = _create(cfg)
+    assert rc == 0
+    for v in (0, 1, 0, 7):
+        assert L.aoh_kv_set_decode_append(h, v) == 0
+    L.aoh_kv_destroy(h)
