@@ -605,13 +605,14 @@ def run_decode(torch, dist, w: dict, args, world: int, rank: int, dev, peaks: di
 # N = 1 extras: prefill, classifier, whole model
 # ----------------------------------------------------------------------------
 
-def prefill_sample(torch, dev, peaks):
+def prefill_sample(torch, dev, peaks, C: int = 4096):
     """bf16 prefill TFLOP/s on a bounded sample of the 64K chunked prefill
-    (Qwen2.5-7B shapes, one layer, 2 of 4 KV heads streaming): the last 4096-token
-    chunk at 61440 cached tokens.  Three launches of about 2 ms: the burst peak."""
+    (Qwen2.5-7B shapes, one layer, 2 of 4 KV heads streaming): the last chunk of
+    C tokens (4096: at 61440 cached tokens, three launches of about 2 ms, so the
+    burst peak; 256: at 65280, the call the 256-token prefill repeats)."""
     from aoh_b200 import AoHKVCache, aoh_attention
     from aoh_b200.metrics import attention_flops
-    Hq, Gq, past, C = 28, 4, 61440, 4096
+    Hq, Gq, past = 28, 4, 65536 - C
     labels = np.array([[1, 0, 1, 0]], dtype=np.float64)
     cache = AoHKVCache(labels, Hq, batch=1, max_context=past + C, dtype=torch.bfloat16, device=dev,
                        reserve_all=True)
@@ -640,7 +641,7 @@ def prefill_sample(torch, dev, peaks):
     cache.close()
     return {"tflops": round(tf, 2), "frac": round(tf / peaks["bf16"], 4), "peak": "bf16 burst (3 launches)",
             "ms": round(sec * 1e3, 3), "flops": flops,
-            "sample": "1 layer, last 4096-token chunk at 61440 cached tokens, Qwen2.5-7B heads, 2/4 streaming"}
+            "sample": f"1 layer, last {C}-token chunk at {past} cached tokens, Qwen2.5-7B heads, 2/4 streaming"}
 
 
 def prefill_full(torch, dev, peaks, chunk: int, context: int = 65536, layers: int = 28):
@@ -967,6 +968,8 @@ def main():
     ap.add_argument("--no-whole-model", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the 8-sequence 256K strong-scaling workload")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sample (profiling)")
+    ap.add_argument("--chunk", type=int, default=4096, choices=[256, 4096],
+                    help="--prefill-only: the sample's chunk (the last chunk of the 64K prefill)")
     ap.add_argument("--whole-model", action="store_true",
                     help="only the whole-model decode ms/token (random-init Llama-3.1-8B, --context tokens)")
     ap.add_argument("--prefill-full", type=int, default=0, metavar="CHUNK",
@@ -991,7 +994,7 @@ def main():
         dev = torch.device("cuda", 0)
         peaks = measured_peaks()
         if args.prefill_only:
-            res = {"prefill": prefill_sample(torch, dev, peaks)}
+            res = {"prefill": prefill_sample(torch, dev, peaks, args.chunk)}
         elif args.whole_model:
             res = {"whole_model": whole_model(torch, dev, context=args.context or 131072)}
         elif args.classifier_only:
