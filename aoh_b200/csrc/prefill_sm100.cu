@@ -96,6 +96,7 @@ __device__ __forceinline__ uint32_t col_s(int q) { return q ? 128u : 0u; }    //
 __device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 256u; }  // O_q
 constexpr int kMaxItemsP = 768;
 constexpr int kMaxSplitP = 32;                        // key-range splits of one retrieval CTA
+constexpr int kMinSplitTiles = 2;                     // key tiles of the longest row block per split, at least
 // One split's partial of one query tile: O / l as bf16, 8 dims per 16 bytes at
 // [dim / 8][row], then m and l (fp32) per row.
 constexpr int kPartBytes = BM * kHeadDim * 2 + 2 * BM * 4;
@@ -110,10 +111,12 @@ struct PrefillArgs {
   // writes a partial to ws, the last to finish (ticket in counters) combines.
   // ws slot = (item * n_qtiles + row block) * n_split + split.
   // Grid (1-D): first every (row block, retrieval item, split) -- row blocks
-  // fastest, so neighbouring CTAs read the same key tiles -- then every
-  // (row block, streaming item): short CTAs that fill the last wave's tail.
+  // fastest, so neighbouring CTAs read the same key tiles; the row-pair items
+  // last, with their ceil(n_qtiles / 2) slots only -- then every (row block,
+  // streaming item): short CTAs that fill the last wave's tail.
   int n_split;
   int n_retr_items;
+  int n_rp_items;  // the last n_rp_items retrieval items are row-pair items
   // 1: the kernel before this one in the stream wrote another layer's pages,
   // so the first cache tiles may be fetched before waiting for it
   int prefetch;
@@ -142,10 +145,10 @@ struct PrefillArgs {
   int* ring_counters;  // one per (sequence, KV head), zero between launches
   int n_items;
   // ((b * Hq + h0) << 3) | (row_pair << 2) | ((tiles - 1) << 1) | retrieval;
-  // retrieval items first.  tiles = 2: heads h0 and h0+1 of one KV group over
-  // the same rows, or (row_pair, retrieval only) head h0 over two adjacent row
-  // blocks -- the leftover head of an odd group; its slots pair row blocks
-  // (n-1-2s, n-2-2s), so slots s >= ceil(n/2) have no work.
+  // retrieval items first (row-pair items at their end).  tiles = 2: heads h0
+  // and h0+1 of one KV group over the same rows, or (row_pair, retrieval only)
+  // head h0 over two adjacent row blocks -- the leftover head of an odd group;
+  // its slots pair row blocks (n-1-2s, n-2-2s), s < ceil(n/2).
   int item[kMaxItemsP];
 };
 
@@ -342,14 +345,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   const CacheGeom& G = a.geom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int heavy = a.n_retr_items * a.n_qtiles;
+  // retrieval slots with work: every row block of a full item, the first
+  // ceil(n_qtiles / 2) slots of a row-pair item
+  const int full_slots = (a.n_retr_items - a.n_rp_items) * a.n_qtiles;
+  const int rp_slots = (a.n_qtiles + 1) / 2;
+  const int heavy_live = full_slots + a.n_rp_items * rp_slots;
   int item_idx, qtile, split;
-  if ((int)blockIdx.x < heavy * a.n_split) {
-    qtile = blockIdx.x % a.n_qtiles;
-    item_idx = (blockIdx.x / a.n_qtiles) % a.n_retr_items;
-    split = blockIdx.x / heavy;
+  if ((int)blockIdx.x < heavy_live * a.n_split) {
+    const int k = blockIdx.x % heavy_live;
+    split = blockIdx.x / heavy_live;
+    if (k < full_slots) {
+      qtile = k % a.n_qtiles;
+      item_idx = k / a.n_qtiles;
+    } else {
+      qtile = (k - full_slots) % rp_slots;
+      item_idx = a.n_retr_items - a.n_rp_items + (k - full_slots) / rp_slots;
+    }
   } else {
-    const int r = blockIdx.x - heavy * a.n_split;
+    const int r = blockIdx.x - heavy_live * a.n_split;
     qtile = r % a.n_qtiles;
     item_idx = a.n_retr_items + r / a.n_qtiles;
     split = 0;
@@ -364,7 +377,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   int i0b = i0;                            // first row of tile 1
   if (row_pair) {
     const int rb = a.n_qtiles - 1 - 2 * qtile;  // the later row block of the pair
-    if (rb < 0) return;                         // a slot past the pairs: no work
+    if (rb < 0) return;                         // (never launched: slots stop at ceil(n / 2))
     i0 = rb * BM;
     i0b = (rb - 1) * BM;
     nq = rb >= 1 ? 2 : 1;
@@ -805,28 +818,35 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         named_bar_sync(3, nq * 128);
         const int r_lo = BM * split / n_split, r_hi = BM * (split + 1) / n_split;
-        const int per_tile = (r_hi - r_lo) * (kHeadDim / 8);
+        // 16 dims x one row per item: with up to 12 splits and 16 rows a tile
+        // each thread has one item and issues every load of it together
+        const int n_rows = r_hi - r_lo, per_tile = n_rows * (kHeadDim / 16);
         for (int it = tid; it < nq * per_tile; it += nq * 128) {
+          // rows fastest: a warp's loads of one split are consecutive 16-byte
+          // chunks of the [dim / 8][row] partial (and consecutive m, l)
           const int qq = it / per_tile, rem = it - qq * per_tile;
-          const int r = r_lo + rem / (kHeadDim / 8), c8 = rem % (kHeadDim / 8);
+          const int r = r_lo + rem % n_rows, c16 = rem / n_rows;
           const uint8_t* p0 = a.ws + ((size_t)gslot * n_split * 2 + qq) * kPartBytes;  // split s at + s * 2 * kPartBytes
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float acc[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = 0.f;
           float M = -INFINITY, L = 0.f;
-          constexpr int kB = 8;
+          constexpr int kB = 12;
           for (int sp = 0; sp < n_split; sp += kB) {
-            uint4 v[kB];
+            uint4 v[kB][2];
             float ms[kB], ls[kB];
 #pragma unroll
             for (int k = 0; k < kB; ++k) {
               ms[k] = -INFINITY;
               ls[k] = 0.f;
-              v[k] = make_uint4(0u, 0u, 0u, 0u);
+              v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
               if (sp + k < n_split) {
                 const uint8_t* ps = p0 + (size_t)(sp + k) * 2 * kPartBytes;
                 const float* qml = reinterpret_cast<const float*>(ps + BM * kHeadDim * 2);
                 ms[k] = __ldcg(qml + r);
                 ls[k] = __ldcg(qml + BM + r);
-                v[k] = __ldcg(reinterpret_cast<const uint4*>(ps) + c8 * BM + r);
+                v[k][0] = __ldcg(reinterpret_cast<const uint4*>(ps) + (2 * c16) * BM + r);
+                v[k][1] = __ldcg(reinterpret_cast<const uint4*>(ps) + (2 * c16 + 1) * BM + r);
               }
             }
 #pragma unroll
@@ -836,11 +856,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
               const float alpha = fast_exp2(M - Mn);
               const float w = fast_exp2(ms[k] - Mn) * ls[k];
               L = fmaf(L, alpha, w);
-              const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                acc[2 * j] = fmaf(w, bf16_lo(u[j]), acc[2 * j] * alpha);
-                acc[2 * j + 1] = fmaf(w, bf16_hi(u[j]), acc[2 * j + 1] * alpha);
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t u[4] = {v[k][h].x, v[k][h].y, v[k][h].z, v[k][h].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  acc[8 * h + 2 * j] = fmaf(w, bf16_lo(u[j]), acc[8 * h + 2 * j] * alpha);
+                  acc[8 * h + 2 * j + 1] = fmaf(w, bf16_hi(u[j]), acc[8 * h + 2 * j + 1] * alpha);
+                }
               }
               M = Mn;
             }
@@ -848,10 +871,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
           const int qi_r = q_row0(qq) + r;
           if (qi_r < a.C) {
             const float inv = L > 0.f ? 1.f / L : 0.f;
-            __nv_bfloat16* d = a.out + (((size_t)b * a.C + qi_r) * G.Hq + q_head(qq)) * kHeadDim + 8 * c8;
-            *reinterpret_cast<uint4*>(d) =
-                make_uint4(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv),
-                           pack_bf16(acc[4] * inv, acc[5] * inv), pack_bf16(acc[6] * inv, acc[7] * inv));
+            __nv_bfloat16* d = a.out + (((size_t)b * a.C + qi_r) * G.Hq + q_head(qq)) * kHeadDim + 16 * c16;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              reinterpret_cast<uint4*>(d)[h] =
+                  make_uint4(pack_bf16(acc[8 * h] * inv, acc[8 * h + 1] * inv),
+                             pack_bf16(acc[8 * h + 2] * inv, acc[8 * h + 3] * inv),
+                             pack_bf16(acc[8 * h + 4] * inv, acc[8 * h + 5] * inv),
+                             pack_bf16(acc[8 * h + 6] * inv, acc[8 * h + 7] * inv));
           }
         }
         // the last split to finish combining makes both counters ready for the next launch
@@ -946,8 +973,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (s_ticket == ((G.grp + 1) / 2) * a.n_qtiles - 1) {
         const int ra_hi = min(a.C, max(0, G.sink - a.T));                         // rows at sink positions
         const int rb_lo = G.ring_cap > 0 ? max(ra_hi, a.C - G.ring_cap) : a.C;  // rows the ring keeps
-        append_rows<8>(a, b, g, false, 0, ra_hi, warp, nq * 4, lane);
-        append_rows<8>(a, b, g, false, rb_lo, a.C, warp, nq * 4, lane);
+        append_rows<16>(a, b, g, false, 0, ra_hi, warp, nq * 4, lane);
+        append_rows<16>(a, b, g, false, rb_lo, a.C, warp, nq * 4, lane);
         if (tid == 0) a.ring_counters[b * G.G + g] = 0;  // ready for the next launch
       }
     }
@@ -1048,24 +1075,28 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   if (rc0) return rc0;
   PrefillArgs a;
   a.n_items = 0;
+  a.n_rp_items = 0;
   const int grp = cf.num_q_heads / cf.num_kv_heads;
-  for (int pass = 0; pass < 2; ++pass)  // retrieval items (heavy) first
+  // retrieval items (heavy) first, their row-pair items last; then streaming items
+  for (int pass = 0; pass < 3; ++pass)
     for (int b = 0; b < cf.batch; ++b)
       for (int g = 0; g < cf.num_kv_heads; ++g) {
         if (!c->owned[c->unit(layer, b, g)]) continue;
         // all_causal (one-shot prefill of the decoding-simulation protocol over
         // an empty cache): every head attends causally to the whole chunk
         const bool r = all_causal || c->retrieval(layer, g);
-        if (r != (pass == 0)) continue;
+        if (r != (pass < 2)) continue;
         for (int j = 0; j < grp; j += 2) {  // pairs of query heads of the group
-          if (a.n_items >= kMaxItemsP)
-            return fail(AOH_ERR_UNSUPPORTED, "prefill: more than %d (sequence, head pair) items", kMaxItemsP);
           const int h0 = g * grp + j;
           const int heads = grp - j >= 2 ? 2 : 1;
           // a retrieval group's leftover head pairs two row blocks instead
           const int row_pair = (heads == 1 && r && q_len > BM) ? 1 : 0;
+          if (r && row_pair != (pass == 1 ? 1 : 0)) continue;
+          if (a.n_items >= kMaxItemsP)
+            return fail(AOH_ERR_UNSUPPORTED, "prefill: more than %d (sequence, head pair) items", kMaxItemsP);
           a.item[a.n_items++] = ((b * cf.num_q_heads + h0) << 3) | (row_pair << 2) |
                                 ((heads - 1 + row_pair) << 1) | (r ? 1 : 0);
+          a.n_rp_items += row_pair;
         }
       }
   if (a.n_items == 0 || q_len == 0) return AOH_OK;
@@ -1081,29 +1112,36 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   // whole grid is one wave the splits of a row block share it (about one
   // period), otherwise the last split reads every partial alone at one SM's
   // L2 rate (about 0.6 period per split).
-  const int heavy = n_retr_items * a.n_qtiles;  // grid slots (row-pair items leave half empty)
-  int heavy_live = 0;
-  for (int i = 0; i < n_retr_items; ++i)
-    heavy_live += (a.item[i] >> 2) & 1 ? (a.n_qtiles + 1) / 2 : a.n_qtiles;
+  const int heavy = n_retr_items * a.n_qtiles;  // scratch slots (a row-pair item uses half of its own)
+  const int heavy_live = (n_retr_items - a.n_rp_items) * a.n_qtiles + a.n_rp_items * ((a.n_qtiles + 1) / 2);
   const int light = (a.n_items - n_retr_items) * a.n_qtiles;
   const int cache_tiles = ((past_len + kPage - 1) / kPage + 7) / 8;
   const int max_tiles = cache_tiles + a.n_qtiles;  // the last row block's list
   // a streaming CTA's list: sink + ring pages, and the window's new rows
   const int light_tiles = (c->sink_pages + c->ring_pages + 7) / 8 + (cf.sink_size + cf.recent_size) / BM + 2;
+  // ... and its length at this call: the sink and ring pages written so far,
+  // the window's new rows (at most recent + one row block), the sink's rows
+  const int str_pages = (std::min(cf.sink_size, past_len) + kPage - 1) / kPage +
+                        (std::min(c->ring_cap, std::max(0, past_len - cf.sink_size)) + kPage - 1) / kPage;
+  const int light_now = (str_pages + 7) / 8 + std::min(a.n_qtiles, (cf.recent_size + BM - 1) / BM + 1) +
+                        (past_len < cf.sink_size ? 1 : 0);
   const int sms = std::max(1, c->num_sms);
   int n_split = 1;
   if (heavy > 0) {
     double best = 0.0;
     for (int sp = 1; sp <= kMaxSplitP; ++sp) {
-      if (sp > 1 && max_tiles / sp < 8) break;  // keep at least 8 tiles per split
+      if (sp > 1 && max_tiles / sp < kMinSplitTiles) break;
       const double waves = std::ceil((double)heavy_live * sp / sms);
       // streaming CTAs run after the split CTAs: in the last wave's free slots
       // if they fit, else as extra short waves
       const double spare = waves * sms - (double)heavy_live * sp;
       const double extra = light > spare ? std::ceil((light - spare) / sms) * light_tiles : 0.0;
-      const bool one_wave = (double)heavy * sp + light <= sms;
+      const bool one_wave = (double)heavy_live * sp + light <= sms;
       const double combine = sp > 1 ? (one_wave ? 1.0 : 0.6 * sp) : 0.0;
-      const double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 2.0 : 1.0)) + extra + combine;
+      double cost = waves * (std::ceil((double)max_tiles / sp) + (sp > 1 ? 2.0 : 1.0)) + extra + combine;
+      // in a single wave the streaming CTAs run beside the split ones: the
+      // launch lasts at least as long as a streaming CTA's list
+      if (waves <= 1.0 && light > 0 && light <= spare) cost = std::max(cost, light_now + 1.0 + combine);
       if (sp == 1 || cost < best * 0.97) {  // split only for a clear gain
         best = cost;
         n_split = sp;
@@ -1114,7 +1152,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.n_retr_items = n_retr_items;
   // every CTA of a one-wave grid is resident at once (one CTA per SM, and the
   // next kernel launches only after all of them have started)
-  a.coop = n_split > 1 && heavy * n_split + light <= sms ? 1 : 0;
+  a.coop = n_split > 1 && heavy_live * n_split + light <= sms ? 1 : 0;
   a.append = all_causal ? 0 : 1;
   a.prefetch = c->last_write_layer != layer ? 1 : 0;
   c->last_write_layer = layer;  // the kernel appends this call's rows to the layer's pages
@@ -1163,7 +1201,7 @@ int launch_prefill_bf16(aoh_kv_cache* c, int layer, int past_len, int q_len, con
   a.C = q_len;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)kHeadDim));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(heavy * n_split + light, 1, 1);
+  cfg.gridDim = dim3(heavy_live * n_split + light, 1, 1);
   cfg.blockDim = dim3(kPThreads, 1, 1);
   cfg.dynamicSmemBytes = kPSmem;
   cfg.stream = st;
