@@ -338,9 +338,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
   __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2];
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
-  // [softmax group][buffer][column]: rows [x, y] of this CTA allowed to see the
-  // key of that column of a masked tile (y < x: none)
-  __shared__ char2 s_kwin[2][2][BN];
+  // [softmax group][buffer][column]: the rows of this CTA allowed to see the
+  // key of that column of a masked tile, as the first allowed row and the
+  // count of further allowed rows (lo = 255, len = 0: none), one byte each, so
+  // a thread reads 16 columns' windows with two 16-byte loads
+  __shared__ __align__(16) uint8_t s_klo[2][2][BN];
+  __shared__ __align__(16) uint8_t s_klen[2][2][BN];
   __shared__ int s_ticket;
 
   const CacheGeom& G = a.geom;
@@ -668,7 +671,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       tc_fence_after();
       const bool full = tl.full_for(t_begin + i, i0q);
-      const char2* kw = s_kwin[q][n_masked & 1];
+      const int kbuf = n_masked & 1;
       if (!full) {
         // thread r resolves column r's key once for the group: the rows that
         // may see it are [p - q0, p + recent - q0] (no upper bound for
@@ -680,11 +683,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int q0 = a.T + i0q;
         int lo = max(kpos - q0, 0);
         int hi = (retr || kpos < tl.sink) ? BM - 1 : min(kpos + tl.recent - q0, BM - 1);
-        if (kpos < 0 || lo > BM - 1 || hi < lo) {
-          lo = BM - 1;
-          hi = -128;
-        }
-        s_kwin[q][n_masked & 1][row] = make_char2((signed char)lo, (signed char)hi);
+        const bool none = kpos < 0 || lo > BM - 1 || hi < lo;
+        s_klo[q][kbuf][row] = none ? 255 : (uint8_t)lo;
+        s_klen[q][kbuf][row] = none ? 0 : (uint8_t)(hi - lo);
         named_bar_sync(1 + q, 128);
         ++n_masked;
       }
@@ -693,10 +694,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
       for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_col + 32 * c, sv + 32 * c);
       tc_wait_ld();
       if (!full) {
+        // column e is allowed for this row when (row - lo_e) mod 256 <= len_e
+        // (lo_e = 255 masks every row: row + 1 > 0)
+        const uint4* lo4 = reinterpret_cast<const uint4*>(s_klo[q][kbuf]);
+        const uint4* ln4 = reinterpret_cast<const uint4*>(s_klen[q][kbuf]);
 #pragma unroll
-        for (int e = 0; e < BN; ++e) {
-          const char2 w = kw[e];
-          if (row < w.x || row > w.y) sv[e] = __float_as_uint(-INFINITY);
+        for (int v = 0; v < BN / 16; ++v) {
+          const uint4 L4 = lo4[v], N4 = ln4[v];
+          const uint32_t lw[4] = {L4.x, L4.y, L4.z, L4.w}, nw[4] = {N4.x, N4.y, N4.z, N4.w};
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const uint32_t lo = (lw[k >> 2] >> (8 * (k & 3))) & 0xffu;
+            const uint32_t len = (nw[k >> 2] >> (8 * (k & 3))) & 0xffu;
+            if ((((uint32_t)row - lo) & 0xffu) > len) sv[16 * v + k] = __float_as_uint(-INFINITY);
+          }
         }
       }
       // row max of the raw scores (the scale is positive): 8 independent
