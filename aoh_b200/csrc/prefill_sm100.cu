@@ -239,7 +239,9 @@ struct TileList {
   // true when every (query row of the block starting at row i0q <= i0, key of
   // tile j) pair is allowed
   __device__ __forceinline__ bool full_for(int j, int i0q) const {
-    if (!retr) return false;
+    // streaming: a cache tile of written sink positions only (every query sees
+    // the sink: its positions are below T)
+    if (!retr) return is_cache(j) && (j * 8 + 8) * kPage <= min(sink, T);
     if (is_cache(j)) return (j * 8 + 8) * kPage <= T;
     int r0, lo, hi;
     chunk(j, &r0, &lo, &hi);
