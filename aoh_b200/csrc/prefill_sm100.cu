@@ -22,10 +22,12 @@
 //
 // Work split: retrieval CTAs may be cut into key ranges (split-KV) so short
 // chunks fill the GPU; each range writes a partial (O / l in bf16, m and l in
-// fp32: the combining CTA reads them at one SM's bandwidth, so their size is
-// its time) and the last to finish combines (ticket).  The 1-D grid lists the
-// split CTAs first and the short streaming CTAs last, so the latter fill the
-// final wave.
+// fp32).  When the whole grid is one wave, every range of a row block waits
+// (bounded) for its siblings' partials and combines its own share of the
+// rows; otherwise the last to finish combines all of them (ticket) at one
+// SM's bandwidth.  The 1-D grid lists the split CTAs first (the odd group's
+// row-pair items last among them, with only their live slots) and the short
+// streaming CTAs last, so the latter fill the final wave.
 //
 // Append: the kernel also writes this call's k/v rows into the layer's pages,
 // so no second kernel sits between two layers' prefills.  Retrieval rows (and
